@@ -1,0 +1,599 @@
+"""Benchmark of the batched-FFT hot path: one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload real|c2c|rfft2|pruned] [--fft-impl stockham_r8]
+
+The headline workload is the one the metric is quoted on (configs[1] of BASELINE.json): a step
+is rfft then irfft of 4096 rows of 4096 float32 samples, iid U[-1, 1] from a seed, 2^24 points
+per GPU. `value` is the effective bandwidth of the whole job, algorithmic bytes / time, with the
+reference's byte convention (4 n + 8 (n/2 + 1) bytes per real row and direction): the inputs are
+resident on the device when timing starts, every launch goes through the C ABI
+(include/spectral_b200.h), and the time is device time from CUDA events, the maximum over ranks.
+
+L2 hygiene: 4 rotating buffer sets of 192 MiB each (768 MiB, 6x the 126 MB L2). Step k
+transforms set k mod 4 forward and, for the inverse, reads the spectrum of set (k + 2) mod 4,
+written two steps (and 384 MiB of traffic) earlier, so no kernel reads what the previous kernel
+just wrote.
+
+Multi-GPU (torchrun, one rank per GPU): every rank transforms its own 2^24 points (weak
+scaling, batch sharding with no communication); a barrier and a synchronize bracket the timed
+steps, and the slowest rank's time counts.
+
+Also on the line: `roofline` (the dominant kernel's achieved bytes / its average CUDA-event
+duration against the measured HBM copy peak), `e2e` (the same metric through the public torch
+API with host buffers: pinned host -> device, both transforms, device -> host, every step),
+`cpu_baseline` (the float64 oracle, numpy's pocketfft as in the reference's CPU path, on the
+host's cores), `clocks` (nvidia-smi sampled during the timed steps) and `gpu_launches`.
+
+--impl reference times the reference's CPU implementation of the path (the oracle port) on all
+host cores, with the same workload, metric and unit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "gpu-spectral-stack_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+METRIC = "Effective FFT GB/s (% of B200 HBM peak) at 2^24 pts/GPU, 1/2/4/8 GPUs"
+UNIT = "GB/s"
+SETS = 4
+
+
+def parse() -> argparse.Namespace:
+    p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["real", "c2c", "rfft2", "pruned"], default="real")
+    p.add_argument("--fft-impl", default="stockham_r8", help="registry name (spectral.FFT_IMPLS)")
+    p.add_argument("--columns", default="strided", help="rfft2 workload: strided or transpose")
+    p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    return p.parse_args()
+
+
+# --- workloads -----------------------------------------------------------------------------------
+#
+# Each workload describes one step on one GPU: the synthetic inputs (seeded, BASELINE.json's
+# shapes and distributions), the launches of a step through the C ABI with their algorithmic
+# bytes, the same step through the public torch API, and a CPU sample for the oracle.
+
+
+class Real:
+    """rfft then irfft, n = 4096, batch = 4096, float32 U[-1, 1]."""
+
+    name = "rfft+irfft n=4096 batch=4096 f32 U[-1,1] (configs[1])"
+
+    def __init__(self, impl: str, batch: int = 4096, n: int = 4096):
+        self.impl, self.batch, self.n = impl, batch, n
+        self.w = n // 2 + 1
+        self.bytes_per_call = batch * (4 * n + 8 * self.w)  # 134,250,496 at the headline size
+
+    def host_input(self, seed: int) -> np.ndarray:
+        rng = np.random.default_rng(seed)
+        return rng.uniform(-1.0, 1.0, (self.batch, self.n)).astype(np.float32)
+
+    def device_sets(self, torch, seed: int):
+        sets = []
+        for i in range(SETS):
+            x = torch.from_numpy(self.host_input(seed + i)).cuda()
+            s = torch.empty(self.batch, self.w, dtype=torch.complex64, device="cuda")
+            y = torch.empty_like(x)
+            sets.append((x, s, y))
+        return sets
+
+    def kernels(self) -> list[tuple[str, int]]:
+        return [("rfft", self.bytes_per_call), ("irfft", self.bytes_per_call)]
+
+    def launches_per_step(self) -> int:
+        return 2  # one fused kernel per direction
+
+    def launch(self, native, sets, k: int, stream: int, which: int) -> None:
+        x, s, _ = sets[k % SETS]
+        _, s_old, y = sets[(k + 2) % SETS]
+        imp = self.impl.encode()
+        if which == 0:
+            native.call("spectral_r2c", imp, x.data_ptr(), s.data_ptr(), self.n, self.batch, None, stream)
+        else:
+            native.call("spectral_c2r", imp, s_old.data_ptr(), y.data_ptr(), self.n, self.batch, None, stream)
+
+    def api_step(self, spectral, x_dev):
+        return spectral.irfft(spectral.rfft(x_dev, impl=self.impl), self.n, impl=self.impl)
+
+    def io_bytes(self) -> tuple[int, int]:
+        return self.batch * self.n * 4, self.batch * self.n * 4
+
+    def cpu_step(self, ref, x: np.ndarray) -> None:
+        ref.irfft(ref.rfft(x), self.n)
+
+    def cpu_rows_bytes(self, rows: int) -> int:
+        return 2 * rows * (4 * self.n + 8 * self.w)
+
+
+class C2c:
+    """fft_c2c forward then inverse, n = 1024, batch = 16384, complex64 N(0, 1)."""
+
+    name = "fft_c2c fwd+inv n=1024 batch=16384 c64 N(0,1) (configs[0])"
+
+    def __init__(self, impl: str, batch: int = 16384, n: int = 1024):
+        self.impl, self.batch, self.n = impl, batch, n
+        self.bytes_per_call = 16 * batch * n
+
+    def host_input(self, seed: int) -> np.ndarray:
+        rng = np.random.default_rng(seed)
+        return (rng.standard_normal((self.batch, self.n)) + 1j * rng.standard_normal((self.batch, self.n))).astype(np.complex64)
+
+    def device_sets(self, torch, seed: int):
+        sets = []
+        for i in range(SETS):
+            x = torch.from_numpy(self.host_input(seed + i)).cuda()
+            sets.append((x, torch.empty_like(x), torch.empty_like(x)))
+        return sets
+
+    def kernels(self):
+        return [("fft_fwd", self.bytes_per_call), ("fft_inv", self.bytes_per_call)]
+
+    def launches_per_step(self) -> int:
+        return 2
+
+    def launch(self, native, sets, k, stream, which):
+        x, f, _ = sets[k % SETS]
+        _, f_old, y = sets[(k + 2) % SETS]
+        imp = self.impl.encode()
+        if which == 0:
+            native.call("spectral_c2c", imp, x.data_ptr(), f.data_ptr(), self.n, self.batch, 0, stream)
+        else:
+            native.call("spectral_c2c", imp, f_old.data_ptr(), y.data_ptr(), self.n, self.batch, 1, stream)
+
+    def api_step(self, spectral, x_dev):
+        return spectral.fft_c2c(spectral.fft_c2c(x_dev, impl=self.impl), inverse=True, impl=self.impl)
+
+    def io_bytes(self):
+        return self.batch * self.n * 8, self.batch * self.n * 8
+
+    def cpu_step(self, ref, x):
+        ref.ifft(ref.fft(x))
+
+    def cpu_rows_bytes(self, rows):
+        return 2 * 16 * rows * self.n
+
+
+class Rfft2:
+    """rfft2 then irfft2 of 256 fields of 256 x 256 float32 N(0, 1)."""
+
+    def __init__(self, impl: str, columns: str, batch: int = 256, n1: int = 256, n2: int = 256):
+        self.impl, self.batch, self.n1, self.n2, self.columns = impl, batch, n1, n2, columns
+        self.w = n2 // 2 + 1
+        self.bytes_per_call = batch * (4 * n1 * n2 + 8 * n1 * self.w)
+        self.name = f"rfft2+irfft2 256 x 256x256 f32 N(0,1) columns={columns} (configs[2])"
+        self.method = 1 if columns == "strided" else 0
+
+    def host_input(self, seed):
+        rng = np.random.default_rng(seed)
+        return rng.standard_normal((self.batch, self.n1, self.n2)).astype(np.float32)
+
+    def device_sets(self, torch, seed):
+        from spectral import native
+
+        imp = self.impl.encode()
+        wf = native.workspace("spectral_fft2_r2c_workspace", imp, self.method, self.n1, self.n2, self.batch)
+        wi = native.workspace("spectral_fft2_c2r_workspace", imp, self.method, self.n1, self.n2, self.batch)
+        self.work = torch.empty(max(wf, wi, 1), dtype=torch.complex64, device="cuda")
+        sets = []
+        for i in range(SETS):
+            x = torch.from_numpy(self.host_input(seed + i)).cuda()
+            s = torch.empty(self.batch, self.n1, self.w, dtype=torch.complex64, device="cuda")
+            sets.append((x, s, torch.empty_like(x)))
+        return sets
+
+    def kernels(self):
+        return [("rfft2", self.bytes_per_call), ("irfft2", self.bytes_per_call)]
+
+    def launches_per_step(self) -> int:
+        return 4 if self.method == 1 else 8  # rows + columns, or rows, transpose, rows, transpose
+
+    def launch(self, native, sets, k, stream, which):
+        x, s, _ = sets[k % SETS]
+        _, s_old, y = sets[(k + 2) % SETS]
+        imp = self.impl.encode()
+        if which == 0:
+            native.call("spectral_fft2_r2c", imp, self.method, x.data_ptr(), s.data_ptr(), self.n1,
+                        self.n2, self.batch, self.work.data_ptr(), stream)
+        else:
+            native.call("spectral_fft2_c2r", imp, self.method, s_old.data_ptr(), y.data_ptr(), self.n1,
+                        self.n2, self.batch, self.work.data_ptr(), stream)
+
+    def api_step(self, spectral, x_dev):
+        s = spectral.rfft2(x_dev, impl=self.impl, columns=self.columns)
+        return spectral.irfft2(s, self.n2, impl=self.impl, columns=self.columns)
+
+    def io_bytes(self):
+        return self.batch * self.n1 * self.n2 * 4, self.batch * self.n1 * self.n2 * 4
+
+    def cpu_step(self, ref, x):
+        ref.irfft2(ref.rfft2(x), (self.n1, self.n2))
+
+    def cpu_rows_bytes(self, rows):
+        return 2 * rows * (4 * self.n1 * self.n2 + 8 * self.n1 * self.w)
+
+
+class Pruned:
+    """the FNO layer, 64 samples x 64 channels of 128 x 128 float32 N(0, 1):
+    rfft2_truncated (m1 = m2 = 16), per-mode contraction 64 -> 64 (W iid N(0, 1/4096) per part),
+    irfft2_from_modes."""
+
+    name = "FNO layer: rfft2_truncated + mode_contract + irfft2_from_modes, 64x64x128x128 f32 (configs[3])"
+
+    def __init__(self, impl: str, samples: int = 64, channels: int = 64, n: int = 128, m: int = 16):
+        self.impl, self.samples, self.channels, self.n, self.m = impl, samples, channels, n, m
+        self.fields = samples * channels
+        self.bytes_per_call = self.fields * (4 * n * n + 16 * m * m)
+        modes = 2 * m * m
+        self.contract_bytes = 8 * modes * (2 * self.fields + channels * channels)
+
+    def host_input(self, seed):
+        rng = np.random.default_rng(seed)
+        return rng.standard_normal((self.samples, self.channels, self.n, self.n)).astype(np.float32)
+
+    def device_sets(self, torch, seed):
+        from spectral import native
+
+        rng = np.random.default_rng(seed + 100)
+        shape = (self.channels, self.channels, 2 * self.m, self.m)
+        wv = (rng.standard_normal(shape) + 1j * rng.standard_normal(shape)) / 64.0
+        self.weights = torch.from_numpy(wv.astype(np.complex64)).cuda()
+        imp = self.impl.encode()
+        a = native.workspace("spectral_rfft2_modes_workspace", imp, self.n, self.n, self.m, self.m, self.fields)
+        b = native.workspace("spectral_irfft2_modes_workspace", imp, self.n, self.n, self.m, self.m, self.fields)
+        self.work = torch.empty(max(a, b, 1), dtype=torch.complex64, device="cuda")
+        sets = []
+        for i in range(SETS):
+            x = torch.from_numpy(self.host_input(seed + i)).cuda()
+            modes = torch.empty(self.samples, self.channels, 2 * self.m, self.m, dtype=torch.complex64, device="cuda")
+            mixed = torch.empty_like(modes)
+            sets.append((x, modes, mixed, torch.empty_like(x)))
+        return sets
+
+    def kernels(self):
+        return [("rfft2_modes", self.bytes_per_call), ("mode_contract", self.contract_bytes),
+                ("irfft2_modes", self.bytes_per_call)]
+
+    def launches_per_step(self) -> int:
+        return 5  # pruned rows + pruned columns, the contraction, pruned columns + pruned rows
+
+    def launch(self, native, sets, k, stream, which):
+        x, modes, mixed, _ = sets[k % SETS]
+        _, _, mixed_old, y = sets[(k + 2) % SETS]
+        imp = self.impl.encode()
+        if which == 0:
+            native.call("spectral_rfft2_modes", imp, x.data_ptr(), modes.data_ptr(), self.n, self.n,
+                        self.m, self.m, self.fields, self.work.data_ptr(), stream)
+        elif which == 1:
+            native.call("spectral_mode_contract", modes.data_ptr(), self.weights.data_ptr(),
+                        mixed.data_ptr(), self.samples, self.channels, self.channels, 2 * self.m * self.m, stream)
+        else:
+            native.call("spectral_irfft2_modes", imp, mixed_old.data_ptr(), y.data_ptr(), self.n, self.n,
+                        self.m, self.m, self.fields, self.work.data_ptr(), stream)
+
+    def api_step(self, spectral, x_dev):
+        modes = spectral.rfft2_truncated(x_dev, self.m, self.m, impl=self.impl)
+        mixed = spectral.mode_contract(modes, self.weights)
+        return spectral.irfft2_from_modes(mixed, (self.n, self.n), impl=self.impl)
+
+    def io_bytes(self):
+        return self.fields * self.n * self.n * 4, self.fields * self.n * self.n * 4
+
+    def cpu_step(self, ref, x):
+        modes = ref.rfft2_truncate(x, self.m, self.m)
+        ref.irfft2_from_modes(modes, (self.n, self.n))
+
+    def cpu_rows_bytes(self, rows):  # rows = samples
+        return 2 * rows * self.channels * (4 * self.n * self.n + 16 * self.m * self.m)
+
+
+def make_workload(args):
+    if args.workload == "real":
+        return Real(args.fft_impl)
+    if args.workload == "c2c":
+        return C2c(args.fft_impl)
+    if args.workload == "rfft2":
+        return Rfft2(args.fft_impl, args.columns)
+    return Pruned(args.fft_impl)
+
+
+# --- peaks, clocks, profiles ---------------------------------------------------------------------
+
+
+def hbm_peak() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(kernel: str, workload: str) -> float | None:
+    """DRAM bytes per launch of `kernel` from a committed ncu summary, or None. The summaries
+    under profiles/ carry a line `traffic <workload> <kernel> <bytes per launch>`."""
+    for path in sorted((ROOT / "profiles").glob("*.md")):
+        for line in path.read_text().splitlines():
+            parts = line.strip().strip("`").split()
+            if len(parts) == 4 and parts[0] == "traffic" and parts[1] == workload and parts[2] == kernel:
+                try:
+                    return float(parts[3])
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of one GPU's clocks and throttle reasons every 200 ms."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        else:
+            self.lines = []
+
+    def summary(self) -> dict | None:
+        if not self.lines:
+            return None
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --- CPU legs ------------------------------------------------------------------------------------
+
+
+def cpu_time(wl, rows: int, threads: int, reps: int) -> tuple[float, int]:
+    """Seconds per pass of the oracle over `rows` rows (fields, samples) split over `threads`
+    threads (pocketfft releases the GIL), best of `reps`; and the bytes of one pass."""
+    from oracle import reference as ref
+
+    x = wl.host_input(12345)[:rows]
+    shards = np.array_split(x, threads)
+    best = math.inf
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            list(pool.map(lambda s: wl.cpu_step(ref, s), shards))
+            best = min(best, time.perf_counter() - t0)
+    return best, wl.cpu_rows_bytes(rows)
+
+
+def cpu_sample_rows(wl) -> int:
+    if isinstance(wl, Pruned):
+        return 4
+    if isinstance(wl, Rfft2):
+        return 64
+    return 1024
+
+
+def run_reference(args) -> None:
+    """The reference arm: the reference's CPU implementation of the path (float64 numpy
+    pocketfft, restated as oracle/reference.py) on every host core, same workload and metric."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    wl = make_workload(args)
+    threads = os.cpu_count() or 1
+    rows = cpu_sample_rows(wl)
+    for _ in range(max(0, args.warmup)):
+        cpu_time(wl, rows, threads, 1)
+    per_step = []
+    for _ in range(args.steps):
+        t, nbytes = cpu_time(wl, rows, threads, 1)
+        per_step.append(t)
+    t = statistics.median(per_step)
+    value = nbytes / t / 1e9
+    sample = f"{rows} of the workload's rows per step ({nbytes / 2**20:.0f} MiB of algorithmic bytes), median of {args.steps} steps"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * t, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": wl.name, "path": "numpy.fft (pocketfft) float64, the reference's python/spectral/reference.py"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --- our arm -------------------------------------------------------------------------------------
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "ours", "unavailable": "no CUDA device visible"}))
+        return
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    import spectral
+    from spectral import native
+
+    wl = make_workload(args)
+    peak, peak_source = hbm_peak()
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    sets = wl.device_sets(torch, seed=1000 * rank + 1)
+    kernels = wl.kernels()
+
+    def step(k: int, events=None) -> None:
+        for which in range(len(kernels)):
+            if events is not None:
+                events[k][which].record(stream)
+            wl.launch(native, sets, k, sp, which)
+        if events is not None:
+            events[k][len(kernels)].record(stream)
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(kernels) + 1)] for _ in range(args.steps)]
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for k in range(args.steps):
+            step(k, ev)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(stop)
+    per_kernel_ms = [statistics.mean(ev[k][j].elapsed_time(ev[k][j + 1]) for k in range(args.steps))
+                     for j in range(len(kernels))]
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    bytes_per_step = sum(b for _, b in kernels)
+    value = world * bytes_per_step * args.steps / (max_ms * 1e-3) / 1e9
+
+    # The dominant kernel: the largest share of device time.
+    dom = max(range(len(kernels)), key=lambda j: per_kernel_ms[j])
+    dom_name, dom_bytes = kernels[dom]
+    achieved = dom_bytes / (per_kernel_ms[dom] * 1e-3) / 1e9
+    traffic = ncu_traffic(dom_name, args.workload)
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": dom_name,
+                "peak_source": f"{peak_source} (MEASURED_PEAKS.json hbm_gbs, copy)",
+                "per_kernel_us": {n: round(1000 * ms, 2) for (n, _), ms in zip(kernels, per_kernel_ms)}}
+
+    # End to end through the public torch API: host -> device, the step, device -> host.
+    e2e = None
+    if not args.no_e2e:
+        h2d, d2h = wl.io_bytes()
+        hosts = [torch.from_numpy(wl.host_input(7000 + i)).pin_memory() for i in range(2)]
+        outs = [torch.empty_like(h).pin_memory() for h in hosts]
+        for k in range(2):
+            outs[k % 2].copy_(wl.api_step(spectral, hosts[k % 2].cuda(non_blocking=True)), non_blocking=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_stop = torch.cuda.Event(enable_timing=True)
+        e_steps = max(3, min(args.steps, 10))
+        e_start.record(stream)
+        for k in range(e_steps):
+            outs[k % 2].copy_(wl.api_step(spectral, hosts[k % 2].cuda(non_blocking=True)), non_blocking=True)
+        e_stop.record(stream)
+        torch.cuda.synchronize()
+        et = torch.tensor([e_start.elapsed_time(e_stop)], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(world * bytes_per_step * e_steps / (float(et.item()) * 1e-3) / 1e9, 3),
+               "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "steps": e_steps, "path": "spectral.* torch ops -> C ABI, pinned host buffers"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        rows = cpu_sample_rows(wl)
+        cpu_time(wl, rows, threads, 1)
+        t_cpu, nbytes = cpu_time(wl, rows, threads, 3)
+        cpu = {"value": round(nbytes / t_cpu / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"oracle (numpy pocketfft float64) on {rows} rows of the workload, best of 3, {threads} threads"}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": wl.name, "fft_impl": args.fft_impl, "points_per_gpu": 1 << 24,
+                   "parallelism": f"batch-sharded x{world}, no communication",
+                   "l2": "4 rotating buffer sets (6x L2); inverse reads a spectrum written 2 steps earlier",
+                   "pct_hbm_peak": round(100 * value / world / peak, 2)},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": args.steps * wl.launches_per_step(),
+        "clocks": clocks.summary(), "impl": "ours",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

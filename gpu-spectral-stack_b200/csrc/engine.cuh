@@ -1,0 +1,513 @@
+#pragma once
+
+// The register-resident FFT engine shared by every transform in this library.
+//
+// A transform of N points is held by P = N / E threads, E points each, always in registers. It
+// runs in PASSES = ceil(log2 N / log2 E) passes; pass s is a radix-R_s Stockham step done as an
+// in-register R_s-point DFT (dft.cuh), so the only shared-memory traffic is one exchange
+// between consecutive passes: N = 1024 with E = 32 is two passes and one exchange, against the
+// reference's four shared-memory stages with two barriers each (stockham.cuh:177-209, 442-449).
+// With P <= 32 a transform lives inside one warp and its exchanges need only __syncwarp.
+//
+// Layout invariant: before pass 0 and after the last pass, thread t of a transform holds the
+// element at position t + i P in v[i], i = 0 .. E-1. Consecutive threads therefore touch
+// consecutive elements for every i: the global loads and stores of contiguous rows are
+// coalesced with no staging, and the output comes out in natural order.
+//
+// Pass s has radix R = radix(s) and sub-transform length L = span(s) (the product of the
+// earlier radices). Butterfly j = t + b P (b < E / R) reads positions j + r N / R, which are
+// v[b + r E / R]; multiplies input r by W_{L R}^(k r), k = j mod L; runs the R-point DFT; and
+// writes output r to position (j - k) R + k + r L. The small radix (if log2 E does not divide
+// log2 N) goes first, where no twiddles are needed.
+//
+// Exchange layout: position p is stored at pad(p) = p + L * floor(p / (L R)) when L < 16, else
+// at p. For the strided writes of the early passes this puts the 16 threads of a half-warp on
+// 16 different 8-byte bank pairs; the reads of the next pass (consecutive positions) stay
+// conflict-free. The reference's stage store has 4.5 M bank conflicts per 2^24 points
+// (docs/PROFILING.md:129-136); this layout has none for N >= 256.
+//
+// Twiddles live in shared memory, one table per pass after the first: entry r L + k of pass s
+// holds W_{L R}^(k r) = exp(-2 pi i k r / (L R)). Consecutive threads read consecutive entries,
+// so the reads are conflict-free. The tables are filled once per (persistent) CTA, either
+// computed on chip with sincospif (the "computed" variants) or copied from a correctly rounded
+// table built in double precision on the host (the "_table" variant, twiddles.cu).
+
+#include "common.cuh"
+#include "dft.cuh"
+
+namespace spectral::engine {
+
+constexpr int kMinThreads = 256;
+
+// The pass structure of an (N, E) plan as plain functions, so host code (the twiddle tables in
+// twiddles.cu, the launchers) evaluates exactly what the kernels compile in.
+__host__ __device__ constexpr int plan_passes(int n, int e)
+{
+    if (n <= 1) {
+        return 0;
+    }
+    const int ln = ilog2(n);
+    const int le = ilog2(e);
+    return ln / le + (ln % le != 0 ? 1 : 0);
+}
+__host__ __device__ constexpr int plan_radix(int n, int e, int s)
+{
+    if (e <= 1) {
+        return 1;
+    }
+    const int rem = ilog2(n) % ilog2(e);
+    return (rem != 0 && s == 0) ? (1 << rem) : e;
+}
+__host__ __device__ constexpr int plan_span(int n, int e, int s)
+{
+    int l = 1;
+    for (int i = 0; i < s; ++i) {
+        l *= plan_radix(n, e, i);
+    }
+    return l;
+}
+__host__ __device__ constexpr int plan_tw_offset(int n, int e, int s)
+{
+    int o = 0;
+    for (int i = 1; i < s; ++i) {
+        o += plan_radix(n, e, i) * plan_span(n, e, i);
+    }
+    return o;
+}
+__host__ __device__ constexpr int plan_tw_entries(int n, int e)
+{
+    return plan_tw_offset(n, e, plan_passes(n, e));
+}
+
+template <int N_, int E_>
+struct Plan {
+    static constexpr int N = N_;
+    static constexpr int E = E_;
+    static_assert(is_pow2(N) && is_pow2(E) && E <= N && E <= 32 && (N == 1 || E >= 2), "bad plan");
+    static constexpr int P = N / E;  // threads per transform
+    static constexpr int PASSES = plan_passes(N, E);
+    static constexpr int THREADS = cmax(kMinThreads, P);
+    static constexpr int G = THREADS / P;  // transforms per CTA
+
+    __host__ __device__ static constexpr int radix(int s) { return plan_radix(N, E, s); }
+    __host__ __device__ static constexpr int span(int s) { return plan_span(N, E, s); }
+    __host__ __device__ static constexpr int tw_offset(int s) { return plan_tw_offset(N, E, s); }
+    static constexpr int TW = plan_tw_entries(N, E);  // entries of all the pass tables
+
+    // Storage index of position p in the exchange that follows pass s.
+    __host__ __device__ static constexpr int pad(int p, int s)
+    {
+        return span(s) < 16 ? p + span(s) * (p / (span(s) * radix(s))) : p;
+    }
+    __host__ __device__ static constexpr int buffer_entries()
+    {
+        int b = N + 1;
+        for (int s = 0; s + 1 < PASSES; ++s) {
+            b = cmax(b, pad(N - 1, s) + 1);
+        }
+        return b | 1;  // odd: a column of the [slot][position] staging layout spans all banks
+    }
+    static constexpr int BUF = buffer_entries();  // per-transform slot in shared memory
+};
+
+// Barrier over the P threads of one transform.
+template <int P>
+__device__ __forceinline__ void group_sync()
+{
+    if constexpr (P > 32) {
+        __syncthreads();
+    } else if constexpr (P > 1) {
+        __syncwarp();
+    }
+}
+
+// Fills the pass tables: computed on chip (Table == false) or copied from `table`.
+template <class PL, bool Table>
+__device__ __forceinline__ void fill_pass_twiddles(float2* tw, const float2* __restrict__ table)
+{
+    for (int e = threadIdx.x; e < PL::TW; e += blockDim.x) {
+        if constexpr (Table) {
+            tw[e] = table[e];
+        } else {
+            int s = 1;
+            while (s + 1 < PL::PASSES && e >= PL::tw_offset(s + 1)) {
+                ++s;
+            }
+            const int idx = e - PL::tw_offset(s);
+            const int L = PL::span(s);
+            const int LR = L * PL::radix(s);
+            const int r = idx / L;
+            const int k = idx - r * L;
+            // 2 (k r mod L R) / (L R) is a dyadic fraction with at most 15 bits: exact in float.
+            const float a = 2.0f * static_cast<float>((k * r) & (LR - 1)) / static_cast<float>(LR);
+            float sn = 0.0f;
+            float cs = 1.0f;
+            sincospif(a, &sn, &cs);
+            tw[e] = make_float2(cs, -sn);
+        }
+    }
+}
+
+// Exchange addressing. Rows: each transform owns a padded slot, position p at PL::pad(p, s).
+// Columns: C transforms interleaved, position p of column c at p * C + c (the caller offsets
+// `buf` by c), so the C threads that handle one position of C neighbouring columns touch
+// consecutive words.
+template <class PL, int Stride>
+__device__ __forceinline__ int slot_index(int p, int s)
+{
+    if constexpr (Stride == 0) {
+        return PL::pad(p, s);
+    } else {
+        return p * Stride;
+    }
+}
+
+template <int P, bool CtaSync>
+__device__ __forceinline__ void exchange_sync()
+{
+    if constexpr (CtaSync) {
+        __syncthreads();
+    } else {
+        group_sync<P>();
+    }
+}
+
+// One pass of the engine (see the top of this file).
+template <class PL, int S, bool Inv, int B, int Stride, bool CtaSync>
+__device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
+{
+    constexpr int E = PL::E;
+    constexpr int P = PL::P;
+    constexpr int R = PL::radix(S);
+    constexpr int L = PL::span(S);
+    constexpr int Q = E / R;  // butterflies per thread
+    constexpr bool kLast = S == PL::PASSES - 1;
+    constexpr int kTw = PL::tw_offset(S);
+
+#pragma unroll
+    for (int b = 0; b < Q; ++b) {
+        const int j = t + b * P;
+        const int k = j & (L - 1);
+        float2 u[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            u[r] = v[b + r * Q];
+            if constexpr (S > 0) {
+                if (r > 0) {
+                    u[r] = cmul_tw<Inv>(u[r], tw[kTw + r * L + k]);
+                }
+            }
+        }
+        dft::Dft<R, B, Inv>::run(u);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            if constexpr (kLast) {
+                v[b + r * Q] = u[r];
+            } else {
+                buf[slot_index<PL, Stride>((j - k) * R + k + r * L, S)] = u[r];
+            }
+        }
+    }
+    if constexpr (!kLast) {
+        exchange_sync<P, CtaSync>();
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            v[i] = buf[slot_index<PL, Stride>(t + i * P, S)];
+        }
+        exchange_sync<P, CtaSync>();
+    }
+}
+
+template <class PL, bool Inv, int B, int Stride = 0, bool CtaSync = false>
+__device__ __forceinline__ void run_passes(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
+{
+    dft::static_for<0, PL::PASSES>([&](auto s) {
+        pass<PL, decltype(s)::value, Inv, B, Stride, CtaSync>(v, t, buf, tw);
+    });
+}
+
+// --- the row kernel ----------------------------------------------------------------------------
+//
+// Transforms whose elements are contiguous (rows). A CTA holds G transforms side by side and
+// walks the batch with a grid stride (persistent CTAs: the twiddle tables are filled once per
+// CTA). What a transform reads and writes is the Io policy:
+//
+//   template <class PL> static constexpr int extra()     extra shared-memory table entries
+//   template <class PL, bool Table> void prologue(float2* extra, const float2* extra_table)
+//   template <class PL> void load(float2 (&v)[E], const RowCtx&) const
+//   template <class PL, bool Inv> void store(float2 (&v)[E], const RowCtx&) const
+//
+// Loads and stores may stage through shared memory and use __syncthreads(): every thread of a
+// CTA runs the same number of iterations, inactive slots included.
+
+struct RowCtx {
+    long long tf;        // this slot's transform (valid only when `active`)
+    long long tf0;       // the CTA's first transform in this iteration
+    int count;           // active slots in this iteration
+    int g;               // slot within the CTA
+    int t;               // thread within the transform
+    bool active;
+    float2* buf;         // the slot's exchange buffer
+    float2* bufs;        // every slot's buffer (G * BUF entries)
+    const float2* extra; // the Io's shared-memory table
+};
+
+template <class PL, bool Inv, int B, bool Table, class Io>
+__global__ void __launch_bounds__(PL::THREADS)
+    row_kernel(const Io io, long long batch, const float2* __restrict__ tw_table,
+               const float2* __restrict__ extra_table)
+{
+    extern __shared__ float4 smem_raw[];
+    float2* tw = reinterpret_cast<float2*>(smem_raw);
+    float2* extra = tw + PL::TW;
+    float2* bufs = extra + Io::template extra<PL>();
+
+    fill_pass_twiddles<PL, Table>(tw, tw_table);
+    Io::template prologue<PL, Table>(extra, extra_table);
+    __syncthreads();
+
+    const int g = threadIdx.x / PL::P;
+    const int t = threadIdx.x - g * PL::P;
+    for (long long tf0 = static_cast<long long>(blockIdx.x) * PL::G; tf0 < batch;
+         tf0 += static_cast<long long>(gridDim.x) * PL::G) {
+        RowCtx c;
+        c.tf0 = tf0;
+        c.count = static_cast<int>(batch - tf0 < PL::G ? batch - tf0 : PL::G);
+        c.g = g;
+        c.t = t;
+        c.tf = tf0 + g;
+        c.active = g < c.count;
+        c.buf = bufs + g * PL::BUF;
+        c.bufs = bufs;
+        c.extra = extra;
+
+        float2 v[PL::E];
+        io.template load<PL>(v, c);
+        run_passes<PL, Inv, B>(v, t, c.buf, tw);
+        io.template store<PL, Inv>(v, c);
+    }
+}
+
+template <class PL, class Io>
+constexpr std::size_t row_smem_bytes()
+{
+    return sizeof(float2)
+           * (static_cast<std::size_t>(PL::TW) + Io::template extra<PL>()
+              + static_cast<std::size_t>(PL::G) * PL::BUF);
+}
+
+// --- Io policies for rows ----------------------------------------------------------------------
+
+// Complex rows. Unpruned: rows of N in and out. Pruned (the reference's PrunedFns::c2c,
+// fft.hpp:62-78): input rows hold only the first keep_in values (the rest are zero), output rows
+// only the first keep_out values. `scale` multiplies every output (1/N for the inverse).
+struct C2cIo {
+    const float2* x;
+    float2* y;
+    int keep_in;
+    int keep_out;
+    float scale;
+
+    template <class PL>
+    __host__ __device__ static constexpr int extra() { return 0; }
+    template <class PL, bool Table>
+    __device__ static void prologue(float2*, const float2*) {}
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        if (!c.active) {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = make_float2(0.0f, 0.0f);
+            }
+            return;
+        }
+        if (keep_in == PL::N) {
+            const float2* row = x + c.tf * PL::N + c.t;
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = __ldg(row + i * PL::P);
+            }
+        } else {
+            const float2* row = x + c.tf * keep_in;
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                const int pos = c.t + i * PL::P;
+                v[i] = pos < keep_in ? __ldg(row + pos) : make_float2(0.0f, 0.0f);
+            }
+        }
+    }
+
+    template <class PL, bool Inv>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        if (!c.active) {
+            return;
+        }
+        if (keep_out == PL::N) {
+            float2* row = y + c.tf * PL::N + c.t;
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                row[i * PL::P] = Inv ? cscale(v[i], scale) : v[i];
+            }
+        } else {
+            float2* row = y + c.tf * keep_out;
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                const int pos = c.t + i * PL::P;
+                if (pos < keep_out) {
+                    row[pos] = Inv ? cscale(v[i], scale) : v[i];
+                }
+            }
+        }
+    }
+};
+
+// Fills extra[k] = W_{2N}^k = exp(-pi i k / N), k = 0 .. N: the twiddles of the real-transform
+// combine and prepare steps for n = 2N real points.
+template <class PL, bool Table>
+__device__ __forceinline__ void fill_half_turn(float2* w, const float2* __restrict__ table)
+{
+    for (int k = threadIdx.x; k <= PL::N; k += blockDim.x) {
+        if constexpr (Table) {
+            w[k] = table[k];
+        } else {
+            float sn = 0.0f;
+            float cs = 1.0f;
+            sincospif(static_cast<float>(k) / static_cast<float>(PL::N), &sn, &cs);  // exact ratio
+            w[k] = make_float2(cs, -sn);
+        }
+    }
+}
+
+// X[k] of the 2N-point real transform from zk = Z[k mod N], zmk = Z[(N - k) mod N] of the
+// N-point transform of the packed input and w = W_{2N}^k (the standard packing identity, as in
+// the reference's real.cuh:31-42):
+//   E = (Z[k] + conj Z[N-k]) / 2,  O = (Z[k] - conj Z[N-k]) / (2i),  X[k] = E + w O.
+__device__ __forceinline__ float2 r2c_combine(float2 zk, float2 zmk, float2 w)
+{
+    const float ex = 0.5f * (zk.x + zmk.x);
+    const float ey = 0.5f * (zk.y - zmk.y);
+    const float ox = 0.5f * (zk.y + zmk.y);   // O = -i D with D = (Z[k] - conj Z[N-k]) / 2
+    const float oy = -0.5f * (zk.x - zmk.x);
+    return make_float2(ex + fmaf(w.x, ox, -(w.y * oy)), ey + fmaf(w.x, oy, w.y * ox));
+}
+
+// Z[k] = E + i O from xk = X[k], xmk = X[N - k] and w = W_{2N}^k, the inverse of the combine
+// (real.cuh:46-61 in the reference): E = (X[k] + conj X[N-k]) / 2,
+// O = (X[k] - conj X[N-k]) conj(w) / 2. At k = 0 the imaginary parts of X[0] and X[N] are
+// dropped, as numpy and torch do.
+__device__ __forceinline__ float2 c2r_prepare(float2 xk, float2 xmk, float2 w)
+{
+    const float ex = 0.5f * (xk.x + xmk.x);
+    const float ey = 0.5f * (xk.y - xmk.y);
+    const float dx = 0.5f * (xk.x - xmk.x);
+    const float dy = 0.5f * (xk.y + xmk.y);
+    const float ox = fmaf(dx, w.x, dy * w.y);   // D conj(w), w = (c, -s)
+    const float oy = fmaf(dy, w.x, -(dx * w.y));
+    return make_float2(ex - oy, ey + ox);
+}
+
+// Real input rows (the reference's R2cIo, stockham.cuh:273-307): rows of 2N floats read as N
+// complex values (the memory layout is the same), an N-point forward transform, then the
+// combine into the first `keep` (<= N + 1) outputs per row, staged through the slot buffer so
+// each output can read Z[k] and Z[N - k].
+struct R2cIo {
+    const float2* x;  // rows of N packed complex values
+    float2* y;        // rows of `keep` complex outputs
+    int keep;
+
+    template <class PL>
+    __host__ __device__ static constexpr int extra() { return PL::N + 1; }
+    template <class PL, bool Table>
+    __device__ static void prologue(float2* w, const float2* table) { fill_half_turn<PL, Table>(w, table); }
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        C2cIo{x, nullptr, PL::N, PL::N, 1.0f}.template load<PL>(v, c);
+    }
+
+    template <class PL, bool Inv>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        constexpr int N = PL::N;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            c.buf[c.t + i * PL::P] = v[i];
+        }
+        group_sync<PL::P>();
+        if (c.active) {
+            float2* row = y + c.tf * keep;
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                const int k = c.t + i * PL::P;
+                if (k < keep) {
+                    row[k] = r2c_combine(c.buf[k], c.buf[(N - k) & (N - 1)], c.extra[k]);
+                }
+            }
+            if (c.t == 0 && N < keep) {
+                row[N] = r2c_combine(c.buf[0], c.buf[0], c.extra[N]);
+            }
+        }
+        group_sync<PL::P>();
+    }
+};
+
+// Real output rows (the reference's C2rIo, stockham.cuh:314-340): rows of `keep` (<= N + 1)
+// complex inputs, the rest zero; the load prepares Z[k] from X[k] and X[N - k] (an ascending and
+// a descending run, both coalesced), an N-point inverse transform, and the store writes z / N as
+// 2N reals.
+struct C2rIo {
+    const float2* x;  // rows of `keep` complex inputs
+    float2* y;        // rows of N complex values = 2N reals
+    int keep;
+    float scale;      // 1 / N
+
+    template <class PL>
+    __host__ __device__ static constexpr int extra() { return PL::N + 1; }
+    template <class PL, bool Table>
+    __device__ static void prologue(float2* w, const float2* table) { fill_half_turn<PL, Table>(w, table); }
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        constexpr int N = PL::N;
+        const float2 zero = make_float2(0.0f, 0.0f);
+        if (!c.active) {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = zero;
+            }
+            return;
+        }
+        const float2* row = x + c.tf * keep;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const int k = c.t + i * PL::P;
+            float2 xk = k < keep ? __ldg(row + k) : zero;
+            float2 xmk = N - k < keep ? __ldg(row + (N - k)) : zero;
+            if (k == 0) {
+                xk.y = 0.0f;
+                xmk.y = 0.0f;
+            }
+            v[i] = c2r_prepare(xk, xmk, c.extra[k]);
+        }
+    }
+
+    template <class PL, bool Inv>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        if (!c.active) {
+            return;
+        }
+        float2* row = y + c.tf * PL::N + c.t;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            row[i * PL::P] = cscale(v[i], scale);
+        }
+    }
+};
+
+}  // namespace spectral::engine

@@ -1,0 +1,108 @@
+#pragma once
+
+// Row transforms (contiguous rows) of one engine variant: the plan per size, and the launchers
+// that the per-variant translation units (variant_*.cu) instantiate.
+//
+// A variant is (B, Table): B = 2, 4 or 8 is the DFT building block (dft.cuh), Table says
+// whether the twiddle tables are copied from the correctly rounded host tables (true) or
+// computed on chip (false).
+
+#include "engine.cuh"
+#include "launch.cuh"
+#include "twiddles.cuh"
+
+namespace spectral::engine {
+
+// Points per thread for a transform of n points. Large E means few passes and few shared-memory
+// exchanges, but more registers: 32 points keep one transform of up to 1024 points inside one
+// warp with a single exchange; beyond that 16 points keep register use low enough for several
+// CTAs per SM while three passes cover 4096 points.
+__host__ __device__ constexpr int default_e(int n)
+{
+    return n <= 16 ? n : n <= 64 ? 8 : n <= 256 ? 16 : n <= 1024 ? 32 : n <= 8192 ? 16 : 32;
+}
+
+template <int N>
+using PlanFor = Plan<N, default_e(N)>;
+
+template <class PL, bool Inv, int B, bool Table, class Io>
+void launch_rows(const Io& io, long long batch, cudaStream_t stream, const float2* extra_table)
+{
+    if (batch <= 0) {
+        return;
+    }
+    auto kernel = row_kernel<PL, Inv, B, Table, Io>;
+    constexpr std::size_t smem = row_smem_bytes<PL, Io>();
+    static std::atomic<int> cache[kMaxDevices];
+    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E) : nullptr;
+    const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem,
+                                          cache, (batch + PL::G - 1) / PL::G);
+    kernel<<<grid, PL::THREADS, smem, stream>>>(io, batch, tw, extra_table);
+    SPECTRAL_CUDA(cudaGetLastError());
+}
+
+// Calls f(std::integral_constant<int, n>) for a power of two n in [Lo, Hi], else throws.
+template <int Lo, int Hi, class F>
+void dispatch_pow2(int n, F&& f)
+{
+    if constexpr (Lo <= Hi) {
+        if (n == Lo) {
+            f(std::integral_constant<int, Lo>{});
+            return;
+        }
+        dispatch_pow2<Lo * 2, Hi>(n, static_cast<F&&>(f));
+    } else {
+        throw InvalidArgument("unsupported transform size " + std::to_string(n));
+    }
+}
+
+constexpr int kMaxRowN = 4096;  // largest row transform held by one CTA
+
+template <int B, bool Table>
+struct RowEngine {
+    // `batch` complex rows of n points (2 <= n <= 4096). keep (1 .. n) prunes the frequency side:
+    // a forward transform writes only the first keep outputs per row, an inverse one reads only
+    // the first keep inputs per row (the rest are zero). The inverse divides by n.
+    static void c2c(const float2* x, float2* y, int n, long long batch, Direction d, int keep,
+                    cudaStream_t s)
+    {
+        dispatch_pow2<2, kMaxRowN>(n, [&](auto n_) {
+            constexpr int N = decltype(n_)::value;
+            using PL = PlanFor<N>;
+            if (d == Direction::Forward) {
+                launch_rows<PL, false, B, Table>(C2cIo{x, y, N, keep, 1.0f}, batch, s, nullptr);
+            } else {
+                launch_rows<PL, true, B, Table>(C2cIo{x, y, keep, N, 1.0f / N}, batch, s, nullptr);
+            }
+        });
+    }
+
+    // `batch` real rows of n points (2 <= n <= 8192) to rows of `keep` (1 .. n/2 + 1) outputs.
+    static void r2c(const float* x, float2* y, int n, long long batch, int keep, float2* /*work*/,
+                    cudaStream_t s)
+    {
+        dispatch_pow2<1, kMaxRowN>(n / 2, [&](auto m_) {
+            constexpr int M = decltype(m_)::value;
+            using PL = PlanFor<M>;
+            const float2* w = Table ? twiddles::half_turn(M) : nullptr;
+            launch_rows<PL, false, B, Table>(R2cIo{reinterpret_cast<const float2*>(x), y, keep},
+                                             batch, s, w);
+        });
+    }
+
+    // Rows of `keep` (1 .. n/2 + 1) complex inputs, the rest zero, to real rows of n points,
+    // divided by n.
+    static void c2r(const float2* x, float* y, int n, long long batch, int keep, float2* /*work*/,
+                    cudaStream_t s)
+    {
+        dispatch_pow2<1, kMaxRowN>(n / 2, [&](auto m_) {
+            constexpr int M = decltype(m_)::value;
+            using PL = PlanFor<M>;
+            const float2* w = Table ? twiddles::half_turn(M) : nullptr;
+            launch_rows<PL, true, B, Table>(
+                C2rIo{x, reinterpret_cast<float2*>(y), keep, 1.0f / M}, batch, s, w);
+        });
+    }
+};
+
+}  // namespace spectral::engine

@@ -1,0 +1,256 @@
+// Simple grid-stride kernels (see simple.cuh).
+
+#include "simple.cuh"
+
+#include "engine.cuh"
+#include "launch.cuh"
+
+#include <algorithm>
+
+namespace spectral::simple {
+namespace {
+
+constexpr int kBlock = 256;
+
+unsigned grid_for(long long threads)
+{
+    const int device = current_device();
+    const long long cap = static_cast<long long>(device_sm_count(device)) * 16;
+    const long long blocks = (threads + kBlock - 1) / kBlock;
+    return static_cast<unsigned>(std::max(1LL, std::min(blocks, cap)));
+}
+
+__global__ void scale_kernel(const float2* __restrict__ x, float2* __restrict__ y, std::size_t n,
+                             float alpha)
+{
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+    for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += stride) {
+        const float2 v = x[i];
+        y[i] = make_float2(alpha * v.x, alpha * v.y);
+    }
+}
+
+// 32 x 32 tiles through shared memory, one extra column so a warp's column reads of the tile
+// fall in different banks. Reads and writes are both whole rows of 32 values.
+constexpr int kTile = 32;
+constexpr int kTileRows = 8;
+
+__global__ void transpose_kernel(const float2* __restrict__ x, float2* __restrict__ y, int rows,
+                                 int cols, long long batch)
+{
+    __shared__ float2 tile[kTile][kTile + 1];
+    const long long size = static_cast<long long>(rows) * cols;
+    for (long long b = blockIdx.z; b < batch; b += gridDim.z) {
+        const float2* xs = x + b * size;
+        float2* ys = y + b * size;
+        const int c = blockIdx.x * kTile + threadIdx.x;
+        for (int k = threadIdx.y; k < kTile; k += kTileRows) {
+            const int r = blockIdx.y * kTile + k;
+            if (r < rows && c < cols) {
+                tile[k][threadIdx.x] = xs[static_cast<long long>(r) * cols + c];
+            }
+        }
+        __syncthreads();
+        const int r_out = blockIdx.y * kTile + threadIdx.x;
+        for (int k = threadIdx.y; k < kTile; k += kTileRows) {
+            const int c_out = blockIdx.x * kTile + k;
+            if (r_out < rows && c_out < cols) {
+                ys[static_cast<long long>(c_out) * rows + r_out] = tile[threadIdx.x][k];
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Index in `full` (arrays of n1 x w) of mode e of `modes` (arrays of rows x m2).
+__device__ __forceinline__ long long full_index(long long e, int n1, int w, int m1, int m2)
+{
+    const int rows = m1 > 0 ? 2 * m1 : n1;
+    const long long per = static_cast<long long>(rows) * m2;
+    const long long b = e / per;
+    const int rem = static_cast<int>(e - b * per);
+    const int r = rem / m2;
+    const int c = rem - r * m2;
+    const int row = (m1 > 0 && r >= m1) ? r + (n1 - rows) : r;
+    return (b * n1 + row) * static_cast<long long>(w) + c;
+}
+
+__global__ void gather_kernel(const float2* __restrict__ full, float2* __restrict__ modes, int n1,
+                              int w, int m1, int m2, long long total)
+{
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += stride) {
+        modes[e] = full[full_index(e, n1, w, m1, m2)];
+    }
+}
+
+__global__ void scatter_kernel(const float2* __restrict__ modes, float2* __restrict__ full, int n1,
+                               int w, int m1, int m2, long long total)
+{
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += stride) {
+        full[full_index(e, n1, w, m1, m2)] = modes[e];
+    }
+}
+
+// W_{2m}^k, rounded once from double precision.
+__device__ __forceinline__ float2 half_turn(int k, int m)
+{
+    double sn = 0.0;
+    double cs = 1.0;
+    sincospi(static_cast<double>(k) / static_cast<double>(m), &sn, &cs);
+    return make_float2(static_cast<float>(cs), static_cast<float>(-sn));
+}
+
+__global__ void r2c_post_kernel(const float2* __restrict__ z, float2* __restrict__ y, int m,
+                                int keep, long long total)
+{
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += stride) {
+        const long long t = e / keep;
+        const int k = static_cast<int>(e - t * keep);
+        const float2* row = z + t * m;
+        y[e] = engine::r2c_combine(row[k & (m - 1)], row[(m - k) & (m - 1)], half_turn(k, m));
+    }
+}
+
+__global__ void c2r_pre_kernel(const float2* __restrict__ x, float2* __restrict__ z, int m,
+                               int keep, long long total)
+{
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    const float2 zero = make_float2(0.0f, 0.0f);
+    for (long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += stride) {
+        const long long t = e / m;
+        const int k = static_cast<int>(e - t * m);
+        const float2* row = x + t * keep;
+        float2 xk = k < keep ? row[k] : zero;
+        float2 xmk = m - k < keep ? row[m - k] : zero;
+        if (k == 0) {
+            xk.y = 0.0f;
+            xmk.y = 0.0f;
+        }
+        z[e] = engine::c2r_prepare(xk, xmk, half_turn(k, m));
+    }
+}
+
+// y[base + i] = x[base + bitreverse(i)] within each transform of 2^log2n values.
+__global__ void bit_reverse_kernel(const float2* __restrict__ x, float2* __restrict__ y,
+                                   long long total, int log2n)
+{
+    const long long mask = (1LL << log2n) - 1;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += stride) {
+        const long long base = e & ~mask;
+        const unsigned i = static_cast<unsigned>(e & mask);
+        const unsigned r = log2n == 0 ? 0u : (__brev(i) >> (32 - log2n));
+        y[e] = x[base + r];
+    }
+}
+
+// One in-place decimation-in-time stage: blocks of 2h from blocks of h, twiddle W_{2h}^k rounded
+// once from double precision.
+__global__ void radix2_stage_kernel(float2* y, long long butterflies, int log2h, bool inverse)
+{
+    const long long h = 1LL << log2h;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long b = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+         b < butterflies; b += stride) {
+        const long long k = b & (h - 1);
+        const long long i0 = ((b >> log2h) << (log2h + 1)) | k;
+        const long long i1 = i0 + h;
+        double sn = 0.0;
+        double cs = 1.0;
+        sincospi(static_cast<double>(k) / static_cast<double>(h), &sn, &cs);
+        const float2 w = make_float2(static_cast<float>(cs), static_cast<float>(inverse ? sn : -sn));
+        const float2 u = y[i0];
+        const float2 v = cmul(y[i1], w);
+        y[i0] = cadd(u, v);
+        y[i1] = csub(u, v);
+    }
+}
+
+}  // namespace
+
+void scale(const float2* x, float2* y, std::size_t n, float alpha, cudaStream_t s)
+{
+    if (n == 0) {
+        return;
+    }
+    scale_kernel<<<grid_for(static_cast<long long>(n)), kBlock, 0, s>>>(x, y, n, alpha);
+    SPECTRAL_CUDA(cudaGetLastError());
+}
+
+void transpose(const float2* x, float2* y, int rows, int cols, long long batch, cudaStream_t s)
+{
+    if (batch <= 0 || rows <= 0 || cols <= 0) {
+        return;
+    }
+    const dim3 block(kTile, kTileRows);
+    const dim3 grid(static_cast<unsigned>((cols + kTile - 1) / kTile),
+                    static_cast<unsigned>((rows + kTile - 1) / kTile),
+                    static_cast<unsigned>(std::min(batch, 65535LL)));
+    transpose_kernel<<<grid, block, 0, s>>>(x, y, rows, cols, batch);
+    SPECTRAL_CUDA(cudaGetLastError());
+}
+
+void gather_modes(const float2* full, float2* modes, int n1, int w, int m1, int m2, long long batch,
+                  cudaStream_t s)
+{
+    const long long total = batch * (m1 > 0 ? 2 * m1 : n1) * static_cast<long long>(m2);
+    if (total == 0) {
+        return;
+    }
+    gather_kernel<<<grid_for(total), kBlock, 0, s>>>(full, modes, n1, w, m1, m2, total);
+    SPECTRAL_CUDA(cudaGetLastError());
+}
+
+void scatter_modes(const float2* modes, float2* full, int n1, int w, int m1, int m2,
+                   long long batch, cudaStream_t s)
+{
+    SPECTRAL_CUDA(cudaMemsetAsync(full, 0,
+                                  static_cast<std::size_t>(batch) * n1 * w * sizeof(float2), s));
+    const long long total = batch * (m1 > 0 ? 2 * m1 : n1) * static_cast<long long>(m2);
+    if (total == 0) {
+        return;
+    }
+    scatter_kernel<<<grid_for(total), kBlock, 0, s>>>(modes, full, n1, w, m1, m2, total);
+    SPECTRAL_CUDA(cudaGetLastError());
+}
+
+void r2c_post(const float2* z, float2* y, int m, long long batch, int keep, cudaStream_t s)
+{
+    const long long total = batch * keep;
+    r2c_post_kernel<<<grid_for(total), kBlock, 0, s>>>(z, y, m, keep, total);
+    SPECTRAL_CUDA(cudaGetLastError());
+}
+
+void c2r_pre(const float2* x, float2* z, int m, long long batch, int keep, cudaStream_t s)
+{
+    const long long total = batch * m;
+    c2r_pre_kernel<<<grid_for(total), kBlock, 0, s>>>(x, z, m, keep, total);
+    SPECTRAL_CUDA(cudaGetLastError());
+}
+
+void radix2_c2c(const float2* x, float2* y, int n, long long batch, Direction d, cudaStream_t s)
+{
+    const long long total = static_cast<long long>(n) * batch;
+    const int log2n = ilog2(n);
+    bit_reverse_kernel<<<grid_for(total), kBlock, 0, s>>>(x, y, total, log2n);
+    SPECTRAL_CUDA(cudaGetLastError());
+    for (int st = 0; st < log2n; ++st) {
+        radix2_stage_kernel<<<grid_for(total / 2), kBlock, 0, s>>>(y, total / 2, st,
+                                                                   d == Direction::Inverse);
+        SPECTRAL_CUDA(cudaGetLastError());
+    }
+    if (d == Direction::Inverse) {
+        scale(y, y, static_cast<std::size_t>(total), 1.0f / static_cast<float>(n), s);
+    }
+}
+
+}  // namespace spectral::simple

@@ -1,0 +1,27 @@
+#pragma once
+
+// Correctly rounded twiddle tables for the "_table" variants, built in double precision on the
+// host and kept in device memory for the life of the process.
+//
+// The tables live in one statically sized __device__ pool (twiddles.cu): no cudaMalloc is ever
+// made for them. Each table is built and uploaded on first use on each device, under a mutex,
+// with a synchronous copy, so the first call that needs a table on a device must not be inside a
+// CUDA graph capture (the same first-use behaviour as the reference's twiddle_table(),
+// twiddles.cu:17-46 there).
+
+#include "common.cuh"
+
+namespace spectral::twiddles {
+
+// The pass tables of plan (n, e) in the engine's layout (engine.cuh): plan_tw_entries(n, e)
+// entries; entry r L + k of pass s is W_{L R}^(k r) = exp(-2 pi i k r / (L R)).
+const float2* pass_table(int n, int e);
+
+// W_{2n}^k = exp(-pi i k / n) for k = 0 .. n: n + 1 entries (real-transform combine).
+const float2* half_turn(int n);
+
+// W_total^j = exp(-2 pi i j / total) for j = 0 .. count-1 (the four-step inter-pass factors are
+// products of two such tables).
+const float2* turn(long long total, int count);
+
+}  // namespace spectral::twiddles

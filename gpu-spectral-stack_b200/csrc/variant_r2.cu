@@ -1,0 +1,27 @@
+// The register engine with radix-2 DFT building blocks and twiddles computed on chip with sincospif,
+// behind the registry name "stockham_r2". One translation unit per variant, so the
+// variants compile in parallel.
+
+#include "backend.hpp"
+#include "columns.cuh"
+
+namespace spectral {
+namespace {
+
+using Rows = engine::RowEngine<2, false>;
+using Cols = engine::ColumnEngine<2, false>;
+
+void c2c(const float2* x, float2* y, int n, long long batch, Direction d, int keep, cudaStream_t s)
+{
+    if (n <= engine::kMaxRowN) {
+        Rows::c2c(x, y, n, batch, d, keep, s);
+    } else {
+        Cols::fourstep(x, y, n, batch, d, s);
+    }
+}
+
+}  // namespace
+
+const Backend kEngineR2 = {&c2c, &Rows::r2c, &Rows::c2r, &Cols::columns};
+
+}  // namespace spectral

@@ -1,0 +1,148 @@
+/*
+ * spectral_b200.h: the C ABI of the B200-native batched FFT library (libspectral_b200.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (cudaStream_t passed
+ * as void*; NULL is the legacy default stream), runs on the calling thread's current device,
+ * and returns a status code. On failure spectral_last_error() returns the message for the
+ * calling thread. Kernels are enqueued on `stream` and return without synchronizing.
+ *
+ * Conventions are numpy's and torch's (norm="backward"): forward transforms are unnormalized,
+ * inverse ones divide by the number of points. Transforms of a batch are stored back to back.
+ * Complex values are two packed floats (re, im): complex64 / c10::complex<float> / the
+ * reference's cf32 (csrc/common/types.hpp:7-12).
+ *
+ * `impl` names one of the registry's implementations (spectral_impl_name). The registry keeps
+ * the reference's five names, order and size limits (csrc/fft/registry.hpp:28-40): "naive",
+ * "stockham_r2", "stockham_r4", "stockham_r8", "stockham_r8_table".
+ *
+ * Workspaces: the 2D, pruned and (for "naive") real entry points take a caller-allocated `work`
+ * buffer whose size in complex values the matching *_workspace function reports (0 means NULL
+ * is accepted), as the reference's fft2d.hpp:27-36 and pruned.hpp:26-36 do.
+ */
+#ifndef SPECTRAL_B200_H
+#define SPECTRAL_B200_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define SPECTRAL_API __attribute__((visibility("default")))
+#else
+#define SPECTRAL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. INVALID_ARGUMENT is what the reference signals with std::invalid_argument
+ * (Python ValueError); CUDA_ERROR what its CUDA_CHECK signals with std::runtime_error. */
+#define SPECTRAL_OK 0
+#define SPECTRAL_INVALID_ARGUMENT 1
+#define SPECTRAL_CUDA_ERROR 2
+#define SPECTRAL_INTERNAL_ERROR 3
+
+/* Column methods of the 2D transforms (reference: csrc/fft/fft2d.hpp:24, enum Columns). */
+#define SPECTRAL_COLUMNS_TRANSPOSE 0
+#define SPECTRAL_COLUMNS_STRIDED 1
+
+/* The message of the calling thread's last failed call ("" if none). */
+SPECTRAL_API const char* spectral_last_error(void);
+
+/* --- registry (reference: csrc/fft/registry.hpp:14-51, csrc/torch/ops.cpp:422-438) --------- */
+
+/* Number of implementations; their names by index, in registry order; index of a name or -1. */
+SPECTRAL_API int spectral_impl_count(void);
+SPECTRAL_API const char* spectral_impl_name(int index);
+SPECTRAL_API int spectral_impl_find(const char* name);
+
+/* The limits and capabilities of FftImpl (registry.hpp:14-25): largest single-kernel transform
+ * (2D and pruned), largest 1D complex transform, largest real transform, whether it has a
+ * strided column kernel and in-kernel pruning, and whether real transforms need `work`.
+ * Any output pointer may be NULL. */
+SPECTRAL_API int spectral_impl_limits(const char* impl, int* max_n, int* max_c2c_n, int* max_real_n,
+                         int* has_columns, int* has_pruned, int* real_needs_work);
+
+/* --- elementwise (reference: csrc/ops/scale.hpp, scale_c2c) ---------------------------------- */
+
+/* y = alpha * x over `count` complex values. */
+SPECTRAL_API int spectral_scale(const void* x, void* y, size_t count, float alpha, void* stream);
+
+/* --- 1D (reference: csrc/fft/fft.hpp:13-49, C2cFn / R2cFn / C2rFn) --------------------------- */
+
+/* `batch` transforms of n complex points, n a power of two up to the implementation's
+ * max_c2c_n. Out of place: x and y must not overlap. */
+SPECTRAL_API int spectral_c2c(const char* impl, const void* x, void* y, int n, long long batch, int inverse,
+                 void* stream);
+
+/* Real to complex: `batch` rows of n floats to rows of n/2 + 1 complex values, n a power of two
+ * from 2 up to max_real_n. `work` holds spectral_real_workspace() complex values. */
+SPECTRAL_API int spectral_r2c(const char* impl, const float* x, void* y, int n, long long batch, void* work,
+                 void* stream);
+
+/* Complex to real, the inverse of spectral_r2c divided by n; the imaginary parts of the zero and
+ * n/2 frequencies are ignored, as in numpy and torch. */
+SPECTRAL_API int spectral_c2r(const char* impl, const void* x, float* y, int n, long long batch, void* work,
+                 void* stream);
+
+/* Complex values of `work` that spectral_r2c / spectral_c2r need (0 for the engine variants,
+ * which fuse the real-transform step into their kernels). */
+SPECTRAL_API int spectral_real_workspace(const char* impl, int n, long long batch, size_t* count);
+
+/* Column transforms (reference: ColumnsFn, fft.hpp:51-60): `slabs` row-major arrays of n rows by
+ * `cols` columns, back to back; every column is an n-point transform. In place when x == y.
+ * Only implementations with has_columns. */
+SPECTRAL_API int spectral_columns(const char* impl, const void* x, void* y, int n, int cols, long long slabs,
+                     int inverse, void* stream);
+
+/* --- 2D (reference: csrc/fft/fft2d.hpp:27-39) ------------------------------------------------- */
+
+SPECTRAL_API int spectral_fft2_c2c_workspace(const char* impl, int columns, int n1, int n2, long long batch,
+                                size_t* count);
+SPECTRAL_API int spectral_fft2_r2c_workspace(const char* impl, int columns, int n1, int n2, long long batch,
+                                size_t* count);
+SPECTRAL_API int spectral_fft2_c2r_workspace(const char* impl, int columns, int n1, int n2, long long batch,
+                                size_t* count);
+
+/* `batch` arrays of n1 x n2, rows then columns by `columns` (SPECTRAL_COLUMNS_*). */
+SPECTRAL_API int spectral_fft2_c2c(const char* impl, int columns, const void* x, void* y, int n1, int n2,
+                      long long batch, int inverse, void* work, void* stream);
+/* Real (n1 x n2 floats) to complex (n1 x (n2/2 + 1)). */
+SPECTRAL_API int spectral_fft2_r2c(const char* impl, int columns, const float* x, void* y, int n1, int n2,
+                      long long batch, void* work, void* stream);
+/* Complex (n1 x (n2/2 + 1)) to real (n1 x n2 floats), divided by n1 n2. */
+SPECTRAL_API int spectral_fft2_c2r(const char* impl, int columns, const void* x, float* y, int n1, int n2,
+                      long long batch, void* work, void* stream);
+
+/* --- pruned, the FNO transforms (reference: csrc/fft/pruned.hpp:26-43) ------------------------ */
+
+SPECTRAL_API int spectral_c2c_pruned_workspace(const char* impl, int n, int keep, long long batch, size_t* count);
+/* Forward: the first `keep` of the n outputs per transform (x rows of n, y rows of keep).
+ * Inverse: x rows of keep modes, the rest zero, to y rows of n, divided by n. */
+SPECTRAL_API int spectral_c2c_pruned(const char* impl, const void* x, void* y, int n, int keep, long long batch,
+                        int inverse, void* work, void* stream);
+
+SPECTRAL_API int spectral_rfft2_modes_workspace(const char* impl, int n1, int n2, int m1, int m2,
+                                   long long batch, size_t* count);
+SPECTRAL_API int spectral_irfft2_modes_workspace(const char* impl, int n1, int n2, int m1, int m2,
+                                    long long batch, size_t* count);
+/* The (2 m1) x m2 low-frequency modes of each rfft2 of n1 x n2 real values: rows 0 .. m1-1, then
+ * n1-m1 .. n1-1; columns 0 .. m2-1 (spectral.reference.rfft2_truncate). */
+SPECTRAL_API int spectral_rfft2_modes(const char* impl, const float* x, void* modes, int n1, int n2, int m1,
+                         int m2, long long batch, void* work, void* stream);
+/* The inverse: every other mode zero, then irfft2 (spectral.reference.irfft2_from_modes). */
+SPECTRAL_API int spectral_irfft2_modes(const char* impl, const void* modes, float* y, int n1, int n2, int m1,
+                          int m2, long long batch, void* work, void* stream);
+
+/* --- per-mode channel contraction of an FNO spectral convolution --------------------------- */
+
+/* out[b, o, m] = sum_i x[b, i, m] * w[i, o, m] over complex values: x (batch, cin, modes),
+ * w (cin, cout, modes), out (batch, cout, modes), all contiguous. No reference counterpart: the
+ * reference plans it (docs/ROADMAP.md:71-76, tasks 3.3-3.6) but has no implementation. */
+SPECTRAL_API int spectral_mode_contract(const void* x, const void* w, void* out, long long batch, int cin,
+                           int cout, long long modes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECTRAL_B200_H */

@@ -1,0 +1,106 @@
+"""The drop-in boundary, on the CPU: the C-ABI library loads and exports exactly what
+include/spectral_b200.h declares, the registry keeps the reference's names, order and limits,
+and argument checks answer with the reference's messages before any GPU work. No kernels run."""
+
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import spectral
+from spectral import native
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "spectral_b200.h"
+
+
+def declared() -> set[str]:
+    return set(re.findall(r"SPECTRAL_API\s+(?:int|const char\*)\s+(spectral_\w+)", HEADER.read_text()))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = native.lib()
+    names = declared()
+    assert len(names) >= 24
+    for name in names:
+        assert hasattr(lib, name), name
+
+
+def test_ctypes_table_covers_the_header():
+    assert declared() == set(native.SIGNATURES)
+
+
+def test_registry_keeps_the_reference_names_and_order():
+    assert native.impl_names() == (
+        "naive", "stockham_r2", "stockham_r4", "stockham_r8", "stockham_r8_table"
+    )
+    assert spectral.FFT_IMPLS == native.impl_names()
+
+
+@pytest.mark.parametrize(
+    ("impl", "limits"),
+    [
+        ("naive", (1 << 30, 1 << 30, 1 << 30, 0, 0, 1)),
+        ("stockham_r8", (4096, 1 << 24, 8192, 1, 1, 0)),
+        ("stockham_r8_table", (4096, 1 << 24, 8192, 1, 1, 0)),
+    ],
+)
+def test_registry_limits(impl, limits):
+    import ctypes
+
+    out = [ctypes.c_int(-1) for _ in range(6)]
+    native.check(native.lib().spectral_impl_limits(impl.encode(), *[ctypes.byref(o) for o in out]))
+    assert tuple(o.value for o in out) == limits
+
+
+def test_unknown_implementation_is_rejected_by_name():
+    with pytest.raises(ValueError, match="unknown FFT implementation 'nope'"):
+        native.call("spectral_c2c", b"nope", 0, 0, 8, 1, 0, None)
+    assert native.lib().spectral_impl_find(b"nope") == -1
+
+
+@pytest.mark.parametrize(
+    ("fn", "args", "message"),
+    [
+        ("spectral_c2c", (b"stockham_r8", 0, 0, 12, 1, 0, None), "power of two"),
+        ("spectral_c2c", (b"stockham_r8", 0, 0, 1 << 25, 1, 0, None), "up to 16777216"),
+        ("spectral_r2c", (b"stockham_r8", 0, 0, 16384, 1, 0, None), "power of two from 2 to 8192"),
+        ("spectral_fft2_c2c", (b"stockham_r8", 1, 0, 0, 8192, 2, 1, 0, 0, None),
+         "n1 to be a power of two up to 4096"),
+        ("spectral_fft2_c2c", (b"naive", 1, 0, 0, 8, 8, 1, 0, 0, None),
+         "no strided column kernel"),
+        ("spectral_rfft2_modes", (b"stockham_r8", 0, 0, 8, 8, 5, 2, 1, 0, None),
+         "1 <= m1 <= n1/2"),
+        ("spectral_c2c_pruned", (b"stockham_r8", 0, 0, 8, 9, 1, 0, 0, None), "keep must be in"),
+        ("spectral_c2c", (b"stockham_r8", 4096, 4096, 8, 2, 0, None), "must not overlap"),
+    ],
+)
+def test_argument_checks_use_the_reference_messages(fn, args, message):
+    with pytest.raises(ValueError, match=message):
+        native.call(fn, *args)
+
+
+def test_workspace_sizes_follow_the_drivers():
+    # Strided 2D needs none; the transpose method two arrays; the engine's real transforms none;
+    # naive's real transforms batch * n/2 complex values.
+    assert native.workspace("spectral_fft2_c2c_workspace", b"stockham_r8", 1, 16, 32, 3) == 0
+    assert native.workspace("spectral_fft2_c2c_workspace", b"stockham_r8", 0, 16, 32, 3) == 2 * 3 * 16 * 32
+    assert native.workspace("spectral_real_workspace", b"stockham_r8", 4096, 7) == 0
+    assert native.workspace("spectral_real_workspace", b"naive", 4096, 7) == 7 * 2048
+    assert native.workspace("spectral_fft2_c2r_workspace", b"stockham_r8", 1, 8, 16, 2) == 2 * 8 * 9
+
+
+def test_cpu_tensors_are_rejected_by_the_dispatcher():
+    x = torch.zeros(4, dtype=torch.complex64)
+    with pytest.raises(NotImplementedError, match="CPU"):
+        spectral.scale(x, 0.5)
+    with pytest.raises(NotImplementedError, match="CPU"):
+        spectral.fft_c2c(x, impl="stockham_r8")
+
+
+def test_every_operator_schema_is_registered():
+    for op in ["scale", "fft_c2c", "fft_r2c", "fft_c2r", "fft2_c2c", "fft2_r2c", "fft2_c2r",
+               "fft_c2c_pruned", "rfft2_modes", "irfft2_modes", "mode_contract"]:
+        assert hasattr(torch.ops.spectral, op), op
+    schema = str(torch.ops.spectral.fft_c2c.default._schema)
+    assert 'str impl="naive"' in schema and "bool inverse=False" in schema

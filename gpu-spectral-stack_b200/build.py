@@ -111,6 +111,24 @@ def torch_paths() -> tuple[list[str], list[str], bool]:
     return includes, libs, bool(torch._C._GLIBCXX_USE_CXX11_ABI)
 
 
+def host_cxx() -> str:
+    """The host C++ compiler for the torch shim: SPECTRAL_CXX if set, else the g++ on PATH (the
+    one nvcc uses for host code). CXX is deliberately not used: a toolchain wrapper there may link
+    libstdc++ statically, and a shim with a private libstdc++ inside a process that already has the
+    shared one breaks iostream formatting (c10::str of an integer) once both are initialised."""
+    return os.environ.get("SPECTRAL_CXX") or shutil.which("g++") or "g++"
+
+
+def check_shared_libstdcxx(path: Path) -> None:
+    """Fails the build unless `path` links libstdc++ dynamically."""
+    out = subprocess.run(["readelf", "-d", str(path)], capture_output=True, text=True).stdout
+    if "libstdc++.so" not in out:
+        raise RuntimeError(
+            f"{path.name} does not link libstdc++.so dynamically; set SPECTRAL_CXX to a g++ that "
+            "links the shared libstdc++"
+        )
+
+
 def build_torch_shim(lib: Path) -> Path:
     src = CSRC / "torch_ops.cpp"
     suffix = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
@@ -120,7 +138,7 @@ def build_torch_shim(lib: Path) -> Path:
     includes, libdirs, cxx11 = torch_paths()
     py_inc = sysconfig.get_paths()["include"]
     cmd = [
-        os.environ.get("CXX", "g++"),
+        host_cxx(),
         "-shared",
         "-fPIC",
         "-O2",
@@ -147,6 +165,7 @@ def build_torch_shim(lib: Path) -> Path:
         *[f"-Wl,-rpath,{p}" for p in libdirs],
     ]
     run(cmd)
+    check_shared_libstdcxx(out)
     return out
 
 

@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "dft.cuh"
+#include "tma.cuh"
 
 namespace spectral::engine {
 
@@ -288,6 +289,128 @@ __global__ void __launch_bounds__(PL::THREADS)
     }
 }
 
+// --- the staged row kernel --------------------------------------------------------------------
+//
+// The same transforms as row_kernel, with the input of each tile of G transforms brought into
+// shared memory by one bulk copy (cp.async.bulk, the TMA engine) while the CTA computes the
+// previous tile: two stage buffers, each with an mbarrier that the copy completes. A CTA therefore
+// always has its next 16-64 KiB in flight, whatever its occupancy, which is what keeps a
+// persistent FFT kernel at HBM speed: without it every CTA alternates between waiting for its
+// loads and computing, and the SM's memory pipe idles while all its CTAs compute.
+//
+// Once a tile's threads have read their inputs out of a stage buffer, the same buffer serves as
+// the tile's exchange buffer (the padded per-transform slots of row_kernel), so staging costs no
+// shared memory beyond the second buffer. Per tile: a CTA barrier before reissuing the buffer
+// the previous tile used, one after the inputs are read, and the exchanges' own barriers.
+//
+// Io additionally provides
+//   template <class PL> static constexpr int stage_entries()   >= G * BUF and the tile's input
+//   bool stage_src(tf0, count, src&, bytes&, shift&) const    the bulk copy of a tile's input
+//   template <class PL> void load_staged(v, ctx, tile) const  inputs from the staged tile
+
+template <class PL, class Io>
+__host__ __device__ constexpr int stage_entries()
+{
+    return (cmax(PL::G * PL::BUF, Io::template staged_input_entries<PL>()) + 1) & ~1;
+}
+
+template <class PL, bool Inv, int B, bool Table, class Io>
+__global__ void __launch_bounds__(PL::THREADS)
+    staged_row_kernel(const Io io, long long batch, const float2* __restrict__ tw_table,
+                      const float2* __restrict__ extra_table, unsigned* fault)
+{
+    extern __shared__ float4 smem_raw[];
+    constexpr int kExtra = (Io::template extra<PL>() + 1) & ~1;
+    constexpr int kTw = (PL::TW + 1) & ~1;
+    constexpr int kStage = stage_entries<PL, Io>();
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);  // two mbarriers, 16 bytes
+    float2* tw = reinterpret_cast<float2*>(smem_raw + 1);
+    float2* extra = tw + kTw;
+    float2* stages = extra + kExtra;  // 16-byte aligned: every region above is an even count
+
+    fill_pass_twiddles<PL, Table>(tw, tw_table);
+    Io::template prologue<PL, Table>(extra, extra_table);
+    if (threadIdx.x == 0) {
+        tma::mbar_init(&bars[0], 1);
+        tma::mbar_init(&bars[1], 1);
+        tma::fence_mbar_init();
+    }
+    __syncthreads();
+
+    const long long stride = static_cast<long long>(gridDim.x) * PL::G;
+    const long long first = static_cast<long long>(blockIdx.x) * PL::G;
+    auto issue = [&](int s, long long tf0) {
+        const int count = static_cast<int>(batch - tf0 < PL::G ? batch - tf0 : PL::G);
+        const float2* src = nullptr;
+        unsigned bytes = 0;
+        int shift = 0;
+        io.template stage_src<PL>(tf0, count, src, bytes, shift);
+        tma::mbar_arrive_expect_tx(&bars[s], bytes);
+        tma::bulk_g2s(stages + s * kStage, src, bytes, &bars[s]);
+    };
+    if (threadIdx.x == 0 && first < batch) {
+        issue(0, first);
+    }
+
+    const int g = threadIdx.x / PL::P;
+    const int t = threadIdx.x - g * PL::P;
+    int j = 0;
+    for (long long tf0 = first; tf0 < batch; tf0 += stride, ++j) {
+        const int s = j & 1;
+        // The other buffer's previous tile is finished with: every thread orders its generic
+        // accesses to it (the exchanges) before the bulk copy that refills it.
+        tma::fence_proxy_async();
+        __syncthreads();
+        if (threadIdx.x == 0 && tf0 + stride < batch) {
+            issue(s ^ 1, tf0 + stride);
+        }
+        const bool ok = tma::mbar_wait(&bars[s], static_cast<unsigned>(j >> 1) & 1u);
+        if (__syncthreads_or(!ok)) {
+            // A copy never completed: record it, let the copy this CTA issued last drain (also
+            // bounded) so nothing lands in shared memory after the CTA is gone, and stop.
+            if (threadIdx.x == 0) {
+                atomicOr(fault, tma::kFaultWaitTimeout);
+                if (tf0 + stride < batch) {
+                    tma::mbar_wait(&bars[s ^ 1], static_cast<unsigned>((j + 1) >> 1) & 1u);
+                }
+            }
+            return;
+        }
+        float2* stage = stages + s * kStage;
+        RowCtx c;
+        c.tf0 = tf0;
+        c.count = static_cast<int>(batch - tf0 < PL::G ? batch - tf0 : PL::G);
+        c.g = g;
+        c.t = t;
+        c.tf = tf0 + g;
+        c.active = g < c.count;
+        c.buf = stage + g * PL::BUF;
+        c.bufs = stage;
+        c.extra = extra;
+
+        float2 v[PL::E];
+        {
+            const float2* src = nullptr;
+            unsigned bytes = 0;
+            int shift = 0;
+            io.template stage_src<PL>(tf0, c.count, src, bytes, shift);
+            io.template load_staged<PL>(v, c, stage + shift);
+        }
+        __syncthreads();  // every input read before the exchanges reuse the buffer
+        run_passes<PL, Inv, B>(v, t, c.buf, tw);
+        io.template store<PL, Inv>(v, c);
+    }
+}
+
+template <class PL, class Io>
+constexpr std::size_t staged_smem_bytes()
+{
+    return 16
+           + sizeof(float2)
+                 * (static_cast<std::size_t>((PL::TW + 1) & ~1) + ((Io::template extra<PL>() + 1) & ~1)
+                    + 2 * static_cast<std::size_t>(stage_entries<PL, Io>()));
+}
+
 template <class PL, class Io>
 constexpr std::size_t row_smem_bytes()
 {
@@ -312,6 +435,28 @@ struct C2cIo {
     __host__ __device__ static constexpr int extra() { return 0; }
     template <class PL, bool Table>
     __device__ static void prologue(float2*, const float2*) {}
+
+    // Staged (unpruned input only): a tile is count * N contiguous values.
+    template <class PL>
+    __host__ __device__ static constexpr int staged_input_entries() { return PL::G * PL::N; }
+    template <class PL>
+    __device__ __forceinline__ void stage_src(long long tf0, int count, const float2*& src,
+                                              unsigned& bytes, int& shift) const
+    {
+        src = x + tf0 * PL::N;
+        bytes = static_cast<unsigned>(count) * static_cast<unsigned>(PL::N) * 8u;
+        shift = 0;
+    }
+    template <class PL>
+    __device__ __forceinline__ void load_staged(float2 (&v)[PL::E], const RowCtx& c,
+                                                const float2* tile) const
+    {
+        const float2* row = tile + c.g * PL::N + c.t;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            v[i] = c.active ? row[i * PL::P] : make_float2(0.0f, 0.0f);
+        }
+    }
 
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], const RowCtx& c) const
@@ -429,6 +574,24 @@ struct R2cIo {
         C2cIo{x, nullptr, PL::N, PL::N, 1.0f}.template load<PL>(v, c);
     }
 
+    // Staged: a tile is count rows of N packed complex values, contiguous.
+    template <class PL>
+    __host__ __device__ static constexpr int staged_input_entries() { return PL::G * PL::N; }
+    template <class PL>
+    __device__ __forceinline__ void stage_src(long long tf0, int count, const float2*& src,
+                                              unsigned& bytes, int& shift) const
+    {
+        src = x + tf0 * PL::N;
+        bytes = static_cast<unsigned>(count) * static_cast<unsigned>(PL::N) * 8u;
+        shift = 0;
+    }
+    template <class PL>
+    __device__ __forceinline__ void load_staged(float2 (&v)[PL::E], const RowCtx& c,
+                                                const float2* tile) const
+    {
+        C2cIo{x, nullptr, PL::N, PL::N, 1.0f}.template load_staged<PL>(v, c, tile);
+    }
+
     template <class PL, bool Inv>
     __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
     {
@@ -469,6 +632,42 @@ struct C2rIo {
     __host__ __device__ static constexpr int extra() { return PL::N + 1; }
     template <class PL, bool Table>
     __device__ static void prologue(float2* w, const float2* table) { fill_half_turn<PL, Table>(w, table); }
+
+    // Staged: a tile is count rows of `keep` values, contiguous but (keep being odd) starting on an
+    // 8-byte boundary for odd first rows; the copy starts one value early then (shift = 1) and is
+    // rounded up to 16 bytes. The host uses this path only when batch * keep is even, so the
+    // rounded copy never reads past the end of x.
+    template <class PL>
+    __host__ __device__ static constexpr int staged_input_entries() { return PL::G * (PL::N + 1) + 2; }
+    template <class PL>
+    __device__ __forceinline__ void stage_src(long long tf0, int count, const float2*& src,
+                                              unsigned& bytes, int& shift) const
+    {
+        const float2* start = x + tf0 * keep;
+        shift = static_cast<int>((reinterpret_cast<unsigned long long>(start) >> 3) & 1u);
+        src = start - shift;
+        const unsigned values = static_cast<unsigned>(count) * static_cast<unsigned>(keep) + shift;
+        bytes = ((values + 1u) & ~1u) * 8u;
+    }
+    template <class PL>
+    __device__ __forceinline__ void load_staged(float2 (&v)[PL::E], const RowCtx& c,
+                                                const float2* tile) const
+    {
+        constexpr int N = PL::N;
+        const float2 zero = make_float2(0.0f, 0.0f);
+        const float2* row = tile + c.g * keep;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const int k = c.t + i * PL::P;
+            float2 xk = k < keep ? row[k] : zero;
+            float2 xmk = N - k < keep ? row[N - k] : zero;
+            if (k == 0) {
+                xk.y = 0.0f;
+                xmk.y = 0.0f;
+            }
+            v[i] = c.active ? c2r_prepare(xk, xmk, c.extra[k]) : zero;
+        }
+    }
 
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], const RowCtx& c) const

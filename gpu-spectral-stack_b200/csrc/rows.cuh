@@ -41,6 +41,29 @@ void launch_rows(const Io& io, long long batch, cudaStream_t stream, const float
     SPECTRAL_CUDA(cudaGetLastError());
 }
 
+// The staged kernel (bulk-copy prefetch, engine.cuh) for sizes where it pays, when the input
+// satisfies cp.async.bulk's rules: a 16-byte aligned source and whole 16-byte tiles.
+constexpr int kMinStagedN = 64;
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<unsigned long long>(p) & 15u) == 0; }
+
+template <class PL, bool Inv, int B, bool Table, class Io>
+void launch_rows_staged(const Io& io, long long batch, cudaStream_t stream, const float2* extra_table)
+{
+    if (batch <= 0) {
+        return;
+    }
+    auto kernel = staged_row_kernel<PL, Inv, B, Table, Io>;
+    constexpr std::size_t smem = staged_smem_bytes<PL, Io>();
+    static_assert(smem <= 227 * 1024, "staged tile does not fit in shared memory");
+    static std::atomic<int> cache[kMaxDevices];
+    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E) : nullptr;
+    const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem,
+                                          cache, (batch + PL::G - 1) / PL::G);
+    kernel<<<grid, PL::THREADS, smem, stream>>>(io, batch, tw, extra_table, device_fault_word());
+    SPECTRAL_CUDA(cudaGetLastError());
+}
+
 // Calls f(std::integral_constant<int, n>) for a power of two n in [Lo, Hi], else throws.
 template <int Lo, int Hi, class F>
 void dispatch_pow2(int n, F&& f)
@@ -69,10 +92,25 @@ struct RowEngine {
         dispatch_pow2<2, kMaxRowN>(n, [&](auto n_) {
             constexpr int N = decltype(n_)::value;
             using PL = PlanFor<N>;
+            const bool staged = N >= kMinStagedN && aligned16(x);
             if (d == Direction::Forward) {
-                launch_rows<PL, false, B, Table>(C2cIo{x, y, N, keep, 1.0f}, batch, s, nullptr);
+                const C2cIo io{x, y, N, keep, 1.0f};
+                if constexpr (N >= kMinStagedN) {
+                    if (staged) {
+                        launch_rows_staged<PL, false, B, Table>(io, batch, s, nullptr);
+                        return;
+                    }
+                }
+                launch_rows<PL, false, B, Table>(io, batch, s, nullptr);
             } else {
-                launch_rows<PL, true, B, Table>(C2cIo{x, y, keep, N, 1.0f / N}, batch, s, nullptr);
+                const C2cIo io{x, y, keep, N, 1.0f / N};
+                if constexpr (N >= kMinStagedN) {
+                    if (staged && keep == N) {
+                        launch_rows_staged<PL, true, B, Table>(io, batch, s, nullptr);
+                        return;
+                    }
+                }
+                launch_rows<PL, true, B, Table>(io, batch, s, nullptr);
             }
         });
     }
@@ -85,8 +123,14 @@ struct RowEngine {
             constexpr int M = decltype(m_)::value;
             using PL = PlanFor<M>;
             const float2* w = Table ? twiddles::half_turn(M) : nullptr;
-            launch_rows<PL, false, B, Table>(R2cIo{reinterpret_cast<const float2*>(x), y, keep},
-                                             batch, s, w);
+            const R2cIo io{reinterpret_cast<const float2*>(x), y, keep};
+            if constexpr (M >= kMinStagedN) {
+                if (aligned16(x)) {
+                    launch_rows_staged<PL, false, B, Table>(io, batch, s, w);
+                    return;
+                }
+            }
+            launch_rows<PL, false, B, Table>(io, batch, s, w);
         });
     }
 
@@ -99,8 +143,16 @@ struct RowEngine {
             constexpr int M = decltype(m_)::value;
             using PL = PlanFor<M>;
             const float2* w = Table ? twiddles::half_turn(M) : nullptr;
-            launch_rows<PL, true, B, Table>(
-                C2rIo{x, reinterpret_cast<float2*>(y), keep, 1.0f / M}, batch, s, w);
+            const C2rIo io{x, reinterpret_cast<float2*>(y), keep, 1.0f / M};
+            if constexpr (M >= kMinStagedN) {
+                // The copy of a tile is rounded to 16 bytes; with batch * keep even and x aligned
+                // the rounding never reaches past the end of x.
+                if (aligned16(x) && (batch * keep) % 2 == 0) {
+                    launch_rows_staged<PL, true, B, Table>(io, batch, s, w);
+                    return;
+                }
+            }
+            launch_rows<PL, true, B, Table>(io, batch, s, w);
         });
     }
 };

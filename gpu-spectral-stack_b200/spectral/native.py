@@ -34,6 +34,7 @@ _ip = ctypes.POINTER(ctypes.c_int)
 # name -> (restype, argtypes), in the order of include/spectral_b200.h.
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_last_error": (_s, []),
+    "spectral_device_faults": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
     "spectral_impl_count": (_i, []),
     "spectral_impl_name": (_s, [_i]),
     "spectral_impl_find": (_i, [_s]),
@@ -87,6 +88,13 @@ def check(status: int) -> None:
     if status == INVALID_ARGUMENT:
         raise ValueError(message)
     raise RuntimeError(message)
+
+
+def device_faults(clear: bool = True) -> int:
+    """Fault codes kernels recorded on the current device (0: none); see spectral_device_faults."""
+    value = ctypes.c_uint(0)
+    check(lib().spectral_device_faults(ctypes.byref(value), 1 if clear else 0))
+    return value.value
 
 
 def impl_names() -> tuple[str, ...]:

@@ -48,6 +48,13 @@ extern "C" {
 /* The message of the calling thread's last failed call ("" if none). */
 SPECTRAL_API const char* spectral_last_error(void);
 
+/* Fault codes that kernels recorded on the current device since the last clear (0: none), read
+ * with a synchronizing copy; clear != 0 resets them. A kernel whose bounded wait on an
+ * asynchronous copy gave up records SPECTRAL_FAULT_WAIT_TIMEOUT and returns instead of hanging.
+ * No counterpart in the reference, whose kernels have no waits. */
+#define SPECTRAL_FAULT_WAIT_TIMEOUT 1u
+SPECTRAL_API int spectral_device_faults(unsigned* faults, int clear);
+
 /* --- registry (reference: csrc/fft/registry.hpp:14-51, csrc/torch/ops.cpp:422-438) --------- */
 
 /* Number of implementations; their names by index, in registry order; index of a name or -1. */

@@ -55,6 +55,17 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
+@pytest.fixture(autouse=True)
+def no_device_faults(request):
+    """After every GPU test: no kernel may have given up on a bounded wait (tma.cuh)."""
+    yield
+    if "gpu" in request.node.keywords and torch.cuda.is_available():
+        from spectral import native
+
+        torch.cuda.synchronize()
+        assert native.device_faults(clear=True) == 0, "a kernel recorded a wait timeout"
+
+
 @pytest.fixture
 def rng(request) -> np.random.Generator:
     """Seeded from the test's id: every case draws the same numbers in any order."""

@@ -31,6 +31,13 @@ struct Backend {
     // implementation has no column kernel.
     void (*columns)(const float2* x, float2* y, int n, int cols, long long slabs, int m1_in,
                     int m1_out, Direction d, cudaStream_t s);
+    // The pruned 2D real transforms in one kernel per direction, with the intermediate on chip
+    // (pruned2d.cuh), for the shapes `pruned2d_supported` accepts; nullptr when there are none.
+    bool (*pruned2d_supported)(int n1, int n2, int m1, int m2);
+    void (*rfft2_modes)(const float* x, float2* modes, int n1, int n2, int m1, int m2,
+                        long long fields, cudaStream_t s);
+    void (*irfft2_modes)(const float2* modes, float* y, int n1, int n2, int m1, int m2,
+                         long long fields, cudaStream_t s);
 };
 
 // The register engine in its four registry variants (variant_*.cu) and the simple reference-

@@ -307,16 +307,28 @@ std::size_t c2c_pruned_work(const Impl& impl, int n, int, long long batch)
     return impl.has_pruned() ? 0 : count3(batch, 1, n);
 }
 
-std::size_t rfft2_modes_work(const Impl& impl, int n1, int n2, int, int m2, long long batch)
+bool fused_pruned(const Impl& impl, int n1, int n2, int m1, int m2)
 {
+    return impl.backend->pruned2d_supported != nullptr
+           && impl.backend->pruned2d_supported(n1, n2, m1, m2);
+}
+
+std::size_t rfft2_modes_work(const Impl& impl, int n1, int n2, int m1, int m2, long long batch)
+{
+    if (fused_pruned(impl, n1, n2, m1, m2)) {
+        return 0;
+    }
     if (impl.has_pruned()) {
         return count3(batch, n1, m2);
     }
     return count3(batch, n1, n2 / 2 + 1) + fft2_r2c_work(impl, Columns::Transpose, n1, n2, batch);
 }
 
-std::size_t irfft2_modes_work(const Impl& impl, int n1, int n2, int, int m2, long long batch)
+std::size_t irfft2_modes_work(const Impl& impl, int n1, int n2, int m1, int m2, long long batch)
 {
+    if (fused_pruned(impl, n1, n2, m1, m2)) {
+        return 0;
+    }
     if (impl.has_pruned()) {
         return count3(batch, n1, m2);
     }
@@ -543,6 +555,10 @@ int spectral_rfft2_modes(const char* impl, const float* x, void* modes, int n1, 
         auto* ms = static_cast<float2*>(modes);
         auto* ws = static_cast<float2*>(work);
         const cudaStream_t s = as_stream(stream);
+        if (fused_pruned(i, n1, n2, m1, m2)) {
+            i.backend->rfft2_modes(x, ms, n1, n2, m1, m2, batch, s);
+            return;
+        }
         if (i.has_pruned()) {
             i.backend->r2c(x, ws, n2, batch * n1, m2, nullptr, s);                      // n1 x m2
             columns_any(i, ws, ms, n1, m2, batch, 0, m1, Direction::Forward, s);
@@ -565,6 +581,10 @@ int spectral_irfft2_modes(const char* impl, const void* modes, float* y, int n1,
         const auto* ms = static_cast<const float2*>(modes);
         auto* ws = static_cast<float2*>(work);
         const cudaStream_t s = as_stream(stream);
+        if (fused_pruned(i, n1, n2, m1, m2)) {
+            i.backend->irfft2_modes(ms, y, n1, n2, m1, m2, batch, s);
+            return;
+        }
         if (i.has_pruned()) {
             columns_any(i, ms, ws, n1, m2, batch, m1, 0, Direction::Inverse, s);
             i.backend->c2r(ws, y, n2, batch * n1, m2, nullptr, s);                      // m2.. zero

@@ -41,7 +41,9 @@ namespace spectral::engine {
 constexpr int kMinThreads = 256;
 
 // The pass structure of an (N, E) plan as plain functions, so host code (the twiddle tables in
-// twiddles.cu, the launchers) evaluates exactly what the kernels compile in.
+// twiddles.cu, the launchers) evaluates exactly what the kernels compile in. When log2 E does
+// not divide log2 N one pass has a smaller radix: the first (where it needs no twiddles) or, with
+// `small_last`, the last (which leaves two butterflies per thread there, for mirror pairing).
 __host__ __device__ constexpr int plan_passes(int n, int e)
 {
     if (n <= 1) {
@@ -51,49 +53,54 @@ __host__ __device__ constexpr int plan_passes(int n, int e)
     const int le = ilog2(e);
     return ln / le + (ln % le != 0 ? 1 : 0);
 }
-__host__ __device__ constexpr int plan_radix(int n, int e, int s)
+__host__ __device__ constexpr int plan_radix(int n, int e, int s, bool small_last = false)
 {
     if (e <= 1) {
         return 1;
     }
     const int rem = ilog2(n) % ilog2(e);
-    return (rem != 0 && s == 0) ? (1 << rem) : e;
+    const int small_pass = small_last ? plan_passes(n, e) - 1 : 0;
+    return (rem != 0 && s == small_pass) ? (1 << rem) : e;
 }
-__host__ __device__ constexpr int plan_span(int n, int e, int s)
+__host__ __device__ constexpr int plan_span(int n, int e, int s, bool small_last = false)
 {
     int l = 1;
     for (int i = 0; i < s; ++i) {
-        l *= plan_radix(n, e, i);
+        l *= plan_radix(n, e, i, small_last);
     }
     return l;
 }
-__host__ __device__ constexpr int plan_tw_offset(int n, int e, int s)
+__host__ __device__ constexpr int plan_tw_offset(int n, int e, int s, bool small_last = false)
 {
     int o = 0;
     for (int i = 1; i < s; ++i) {
-        o += plan_radix(n, e, i) * plan_span(n, e, i);
+        o += plan_radix(n, e, i, small_last) * plan_span(n, e, i, small_last);
     }
     return o;
 }
-__host__ __device__ constexpr int plan_tw_entries(int n, int e)
+__host__ __device__ constexpr int plan_tw_entries(int n, int e, bool small_last = false)
 {
-    return plan_tw_offset(n, e, plan_passes(n, e));
+    return plan_tw_offset(n, e, plan_passes(n, e), small_last);
 }
 
-template <int N_, int E_>
+template <int N_, int E_, bool SmallLast_ = false>
 struct Plan {
     static constexpr int N = N_;
     static constexpr int E = E_;
+    static constexpr bool SmallLast = SmallLast_;
     static_assert(is_pow2(N) && is_pow2(E) && E <= N && E <= 32 && (N == 1 || E >= 2), "bad plan");
     static constexpr int P = N / E;  // threads per transform
     static constexpr int PASSES = plan_passes(N, E);
     static constexpr int THREADS = cmax(kMinThreads, P);
     static constexpr int G = THREADS / P;  // transforms per CTA
 
-    __host__ __device__ static constexpr int radix(int s) { return plan_radix(N, E, s); }
-    __host__ __device__ static constexpr int span(int s) { return plan_span(N, E, s); }
-    __host__ __device__ static constexpr int tw_offset(int s) { return plan_tw_offset(N, E, s); }
-    static constexpr int TW = plan_tw_entries(N, E);  // entries of all the pass tables
+    __host__ __device__ static constexpr int radix(int s) { return plan_radix(N, E, s, SmallLast); }
+    __host__ __device__ static constexpr int span(int s) { return plan_span(N, E, s, SmallLast); }
+    __host__ __device__ static constexpr int tw_offset(int s) { return plan_tw_offset(N, E, s, SmallLast); }
+    static constexpr int TW = plan_tw_entries(N, E, SmallLast);  // entries of all the pass tables
+    // Two butterflies per thread in the first / last pass: mirror pairing is possible there.
+    static constexpr bool kPairFirst = PASSES >= 1 && E / plan_radix(N, E, 0, SmallLast) == 2;
+    static constexpr bool kPairLast = PASSES >= 1 && E / plan_radix(N, E, PASSES - 1, SmallLast) == 2;
 
     // Storage index of position p in the exchange that follows pass s.
     __host__ __device__ static constexpr int pad(int p, int s)
@@ -149,20 +156,6 @@ __device__ __forceinline__ void fill_pass_twiddles(float2* tw, const float2* __r
     }
 }
 
-// Exchange addressing. Rows: each transform owns a padded slot, position p at PL::pad(p, s).
-// Columns: C transforms interleaved, position p of column c at p * C + c (the caller offsets
-// `buf` by c), so the C threads that handle one position of C neighbouring columns touch
-// consecutive words.
-template <class PL, int Stride>
-__device__ __forceinline__ int slot_index(int p, int s)
-{
-    if constexpr (Stride == 0) {
-        return PL::pad(p, s);
-    } else {
-        return p * Stride;
-    }
-}
-
 template <int P, bool CtaSync>
 __device__ __forceinline__ void exchange_sync()
 {
@@ -173,8 +166,30 @@ __device__ __forceinline__ void exchange_sync()
     }
 }
 
-// One pass of the engine (see the top of this file).
-template <class PL, int S, bool Inv, int B, int Stride, bool CtaSync>
+// The butterflies a thread runs in a pass with Q butterflies per thread. Plain: j = t + b P, so
+// thread t holds positions t + i P, i = b + r Q. Mirror (Q == 2): butterfly t and its mirror
+// 2P - t (thread 0: butterflies 0 and P), which hold each other's positions N - k: the real
+// transforms' combine and prepare steps then pair X[k] with X[N - k] in registers.
+template <bool Mirror, int P>
+__device__ __forceinline__ int butterfly(int t, int b)
+{
+    if constexpr (Mirror) {
+        return b == 0 ? t : (t == 0 ? P : 2 * P - t);
+    } else {
+        return t + b * P;
+    }
+}
+
+// One pass of the engine (see the top of this file), with the register layout of the next pass.
+//
+// Exchange addressing. Rows (Stride == 0): each transform owns a padded slot; position
+// p = (j - k) R + k + r L, k = j mod L, is stored at (j - k) (R + 1) + k + r L when L < 16 (this
+// is p + L floor(p / (L R)): one gap of L after every L R positions) and at p otherwise.
+// Columns (Stride == C): C transforms interleaved, position p of column c at p C + c (the
+// caller offsets `buf` by c). Either way a thread's write indices are one runtime base per
+// butterfly plus compile-time offsets, and for the plain layout L divides P, so k = t mod L
+// and one set of twiddles serves all Q butterflies.
+template <class PL, int S, bool Inv, int B, int Stride, bool CtaSync, bool Mirror, bool MirrorNext>
 __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
 {
     constexpr int E = PL::E;
@@ -184,10 +199,29 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
     constexpr int Q = E / R;  // butterflies per thread
     constexpr bool kLast = S == PL::PASSES - 1;
     constexpr int kTw = PL::tw_offset(S);
+    constexpr bool kPad = Stride == 0 && L < 16;
+    static_assert(!Mirror || Q == 2, "mirror pairing needs two butterflies per thread");
+    static_assert(Mirror || kLast || P % L == 0, "the plain exchange layout needs L to divide P");
+
+    // One twiddle set serves every butterfly when k = t mod L is the same for all of them (L
+    // divides P); otherwise each butterfly has its own.
+    constexpr bool kShared = !Mirror && P % L == 0;
+    constexpr int kSets = (S > 0) ? (kShared ? 1 : Q) : 1;
+    float2 wt[kSets][R];
+    if constexpr (S > 0) {
+#pragma unroll
+        for (int b = 0; b < kSets; ++b) {
+            const int k = butterfly<Mirror, P>(t, b) & (L - 1);
+#pragma unroll
+            for (int r = 1; r < R; ++r) {
+                wt[b][r] = tw[kTw + r * L + k];
+            }
+        }
+    }
 
 #pragma unroll
     for (int b = 0; b < Q; ++b) {
-        const int j = t + b * P;
+        const int j = butterfly<Mirror, P>(t, b);
         const int k = j & (L - 1);
         float2 u[R];
 #pragma unroll
@@ -195,35 +229,78 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
             u[r] = v[b + r * Q];
             if constexpr (S > 0) {
                 if (r > 0) {
-                    u[r] = cmul_tw<Inv>(u[r], tw[kTw + r * L + k]);
+                    u[r] = cmul_tw<Inv>(u[r], wt[kShared ? 0 : b][r]);
                 }
             }
         }
         dft::Dft<R, B, Inv>::run(u);
+        if constexpr (kLast) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            if constexpr (kLast) {
+            for (int r = 0; r < R; ++r) {
                 v[b + r * Q] = u[r];
-            } else {
-                buf[slot_index<PL, Stride>((j - k) * R + k + r * L, S)] = u[r];
+            }
+        } else {
+            const int base = (j - k) * (R + (kPad ? 1 : 0)) + k;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int idx = base + r * L;
+                buf[Stride == 0 ? idx : idx * Stride] = u[r];
             }
         }
     }
+
     if constexpr (!kLast) {
         exchange_sync<P, CtaSync>();
+        constexpr int R2 = PL::radix(S + 1);
+        constexpr int Q2 = E / R2;
+        constexpr int NB2 = PL::N / R2;  // butterflies of the next pass: positions j + r NB2
+        if constexpr (MirrorNext) {
 #pragma unroll
-        for (int i = 0; i < E; ++i) {
-            v[i] = buf[slot_index<PL, Stride>(t + i * P, S)];
+            for (int b = 0; b < Q2; ++b) {
+                const int j = butterfly<true, P>(t, b);
+#pragma unroll
+                for (int r = 0; r < R2; ++r) {
+                    const int q = j + r * NB2;
+                    const int idx = kPad ? q + L * (q / (L * R)) : q;
+                    v[b + r * Q2] = buf[Stride == 0 ? idx : idx * Stride];
+                }
+            }
+        } else if constexpr (kPad && P % (L * R) == 0) {
+            // pad(t + i P) = t + L floor(t / (L R)) + i (P + P / R), since L R divides P.
+            const int base = t + L * (t / (L * R));
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                v[i] = buf[base + i * (P + P / R)];
+            }
+        } else if constexpr (kPad) {
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                const int q = t + i * P;
+                v[i] = buf[q + L * (q / (L * R))];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                const int q = t + i * P;
+                v[i] = buf[Stride == 0 ? q : q * Stride];
+            }
         }
         exchange_sync<P, CtaSync>();
     }
 }
 
-template <class PL, bool Inv, int B, int Stride = 0, bool CtaSync = false>
+// All passes. MirrorFirst / MirrorLast select the mirror layout of the first / last pass: the
+// registers before the first pass (the load) or after the last pass (the store) then hold
+// butterfly-mirror pairs instead of positions t + i P.
+template <class PL, bool Inv, int B, int Stride = 0, bool CtaSync = false, bool MirrorFirst = false,
+          bool MirrorLast = false>
 __device__ __forceinline__ void run_passes(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
 {
-    dft::static_for<0, PL::PASSES>([&](auto s) {
-        pass<PL, decltype(s)::value, Inv, B, Stride, CtaSync>(v, t, buf, tw);
+    dft::static_for<0, PL::PASSES>([&](auto s_) {
+        constexpr int S = decltype(s_)::value;
+        constexpr bool kMirror = (S == 0 && MirrorFirst) || (S == PL::PASSES - 1 && MirrorLast);
+        constexpr bool kMirrorNext = S + 1 == PL::PASSES - 1 && MirrorLast;
+        pass<PL, S, Inv, B, Stride, CtaSync, kMirror, kMirrorNext>(v, t, buf, tw);
     });
 }
 
@@ -284,7 +361,7 @@ __global__ void __launch_bounds__(PL::THREADS)
 
         float2 v[PL::E];
         io.template load<PL>(v, c);
-        run_passes<PL, Inv, B>(v, t, c.buf, tw);
+        run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
         io.template store<PL, Inv>(v, c);
     }
 }
@@ -397,7 +474,7 @@ __global__ void __launch_bounds__(PL::THREADS)
             io.template load_staged<PL>(v, c, stage + shift);
         }
         __syncthreads();  // every input read before the exchanges reuse the buffer
-        run_passes<PL, Inv, B>(v, t, c.buf, tw);
+        run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
         io.template store<PL, Inv>(v, c);
     }
 }
@@ -425,6 +502,8 @@ constexpr std::size_t row_smem_bytes()
 // fft.hpp:62-78): input rows hold only the first keep_in values (the rest are zero), output rows
 // only the first keep_out values. `scale` multiplies every output (1/N for the inverse).
 struct C2cIo {
+    static constexpr bool kMirrorFirst = false;
+    static constexpr bool kMirrorLast = false;
     const float2* x;
     float2* y;
     int keep_in;
@@ -559,6 +638,8 @@ __device__ __forceinline__ float2 c2r_prepare(float2 xk, float2 xmk, float2 w)
 // combine into the first `keep` (<= N + 1) outputs per row, staged through the slot buffer so
 // each output can read Z[k] and Z[N - k].
 struct R2cIo {
+    static constexpr bool kMirrorFirst = false;
+    static constexpr bool kMirrorLast = false;
     const float2* x;  // rows of N packed complex values
     float2* y;        // rows of `keep` complex outputs
     int keep;
@@ -623,6 +704,8 @@ struct R2cIo {
 // a descending run, both coalesced), an N-point inverse transform, and the store writes z / N as
 // 2N reals.
 struct C2rIo {
+    static constexpr bool kMirrorFirst = false;
+    static constexpr bool kMirrorLast = false;
     const float2* x;  // rows of `keep` complex inputs
     float2* y;        // rows of N complex values = 2N reals
     int keep;
@@ -706,6 +789,222 @@ struct C2rIo {
         for (int i = 0; i < PL::E; ++i) {
             row[i * PL::P] = cscale(v[i], scale);
         }
+    }
+};
+
+// --- mirror-paired real transforms -------------------------------------------------------------
+//
+// For plans with two butterflies per thread in the last pass (real-to-complex) or the first pass
+// (complex-to-real), the engine can give each thread butterfly t together with its mirror 2P - t
+// (run_passes' MirrorLast / MirrorFirst), whose positions are exactly the N - k of the first's. The
+// real-transform step, which pairs Z[k] with Z[N - k] (or X[k] with X[N - k]), then happens in
+// registers: no staging of the spectrum in shared memory, no barrier, every input read once, and
+// one twiddle and one complex product for each pair of outputs:
+//   forward  X[k] = E + W^k O,   X[N - k] = conj(E - W^k O)
+//   inverse  Z[k] = E + i O,     Z[N - k] = conj(E - i O),   O = D conj(W^k)
+// with E, O (forward) and E, D (inverse) as in r2c_combine / c2r_prepare.
+
+// Writes X[k] and X[N - k] (only those below `keep`) from zk = Z[k], zmk = Z[N - k], w = W_{2N}^k.
+__device__ __forceinline__ void r2c_pair(float2* row, int n, int k, int keep, float2 zk, float2 zmk,
+                                         float2 w)
+{
+    const float ex = 0.5f * (zk.x + zmk.x);
+    const float ey = 0.5f * (zk.y - zmk.y);
+    const float ox = 0.5f * (zk.y + zmk.y);
+    const float oy = -0.5f * (zk.x - zmk.x);
+    const float wx = fmaf(w.x, ox, -(w.y * oy));
+    const float wy = fmaf(w.x, oy, w.y * ox);
+    if (k < keep) {
+        row[k] = make_float2(ex + wx, ey + wy);
+    }
+    if (n - k != k && n - k < keep) {
+        row[n - k] = make_float2(ex - wx, wy - ey);
+    }
+}
+
+// Z[k] and Z[N - k] from xa = X[k], xb = X[N - k], w = W_{2N}^k.
+__device__ __forceinline__ void c2r_pair(int k, float2 xa, float2 xb, float2 w, float2& zk, float2& zmk)
+{
+    if (k == 0) {
+        xa.y = 0.0f;
+        xb.y = 0.0f;
+    }
+    const float ex = 0.5f * (xa.x + xb.x);
+    const float ey = 0.5f * (xa.y - xb.y);
+    const float dx = 0.5f * (xa.x - xb.x);
+    const float dy = 0.5f * (xa.y + xb.y);
+    const float ox = fmaf(dx, w.x, dy * w.y);
+    const float oy = fmaf(dy, w.x, -(dx * w.y));
+    zk = make_float2(ex - oy, ey + ox);
+    zmk = make_float2(ex + oy, ox - ey);
+}
+
+// Real input rows with the combine in registers (plans with SmallLast and kPairLast).
+struct R2cPairIo {
+    static constexpr bool kMirrorFirst = false;
+    static constexpr bool kMirrorLast = true;
+    const float2* x;
+    float2* y;
+    int keep;
+
+    template <class PL>
+    __host__ __device__ static constexpr int extra() { return PL::N + 1; }
+    template <class PL, bool Table>
+    __device__ static void prologue(float2* w, const float2* table) { fill_half_turn<PL, Table>(w, table); }
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        C2cIo{x, nullptr, PL::N, PL::N, 1.0f}.template load<PL>(v, c);
+    }
+    template <class PL>
+    __host__ __device__ static constexpr int staged_input_entries() { return PL::G * PL::N; }
+    template <class PL>
+    __device__ __forceinline__ void stage_src(long long tf0, int count, const float2*& src,
+                                              unsigned& bytes, int& shift) const
+    {
+        src = x + tf0 * PL::N;
+        bytes = static_cast<unsigned>(count) * static_cast<unsigned>(PL::N) * 8u;
+        shift = 0;
+    }
+    template <class PL>
+    __device__ __forceinline__ void load_staged(float2 (&v)[PL::E], const RowCtx& c,
+                                                const float2* tile) const
+    {
+        C2cIo{x, nullptr, PL::N, PL::N, 1.0f}.template load_staged<PL>(v, c, tile);
+    }
+
+    template <class PL, bool Inv>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        static_assert(PL::kPairLast, "needs two butterflies per thread in the last pass");
+        if (!c.active) {
+            return;
+        }
+        constexpr int N = PL::N;
+        constexpr int P = PL::P;
+        constexpr int R = PL::radix(PL::PASSES - 1);
+        constexpr int NB = N / R;  // = 2P: positions of butterfly j are j + r NB
+        float2* row = y + c.tf * keep;
+        const int t = c.t;
+        if (t != 0) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int k = t + r * NB;
+                r2c_pair(row, N, k, keep, v[2 * r], v[1 + 2 * (R - 1 - r)], c.extra[k]);
+            }
+        } else {
+            r2c_pair(row, N, 0, keep, v[0], v[0], c.extra[0]);  // X[0] and X[N]
+#pragma unroll
+            for (int r = 1; r <= R / 2; ++r) {
+                r2c_pair(row, N, r * NB, keep, v[2 * r], v[2 * (R - r)], c.extra[r * NB]);
+            }
+#pragma unroll
+            for (int r = 0; r < R / 2; ++r) {
+                r2c_pair(row, N, P + r * NB, keep, v[1 + 2 * r], v[1 + 2 * (R - 1 - r)],
+                         c.extra[P + r * NB]);
+            }
+        }
+    }
+};
+
+// Complex rows of `keep` values to real rows with the prepare step in registers (plans with
+// kPairFirst). X[N] (the Nyquist value) is read by thread 0 alone.
+struct C2rPairIo {
+    static constexpr bool kMirrorFirst = true;
+    static constexpr bool kMirrorLast = false;
+    const float2* x;
+    float2* y;
+    int keep;
+    float scale;  // 1 / N
+
+    template <class PL>
+    __host__ __device__ static constexpr int extra() { return PL::N + 1; }
+    template <class PL, bool Table>
+    __device__ static void prologue(float2* w, const float2* table) { fill_half_turn<PL, Table>(w, table); }
+
+    template <class PL, class Get>
+    __device__ __forceinline__ void prepare(float2 (&v)[PL::E], const RowCtx& c, Get&& get) const
+    {
+        static_assert(PL::kPairFirst, "needs two butterflies per thread in the first pass");
+        constexpr int N = PL::N;
+        constexpr int P = PL::P;
+        constexpr int R = PL::radix(0);
+        constexpr int NB = N / R;  // = 2P
+        const int t = c.t;
+        float2 a[R];
+        float2 b[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            a[r] = get(butterfly<true, P>(t, 0) + r * NB);
+            b[r] = get(butterfly<true, P>(t, 1) + r * NB);
+        }
+        if (t != 0) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int k = t + r * NB;
+                c2r_pair(k, a[r], b[R - 1 - r], c.extra[k], v[2 * r], v[1 + 2 * (R - 1 - r)]);
+            }
+        } else {
+            float2 unused;
+            c2r_pair(0, a[0], get(N), c.extra[0], v[0], unused);
+#pragma unroll
+            for (int r = 1; r <= R / 2; ++r) {
+                c2r_pair(r * NB, a[r], a[R - r], c.extra[r * NB], v[2 * r], v[2 * (R - r)]);
+            }
+#pragma unroll
+            for (int r = 0; r < R / 2; ++r) {
+                c2r_pair(P + r * NB, b[r], b[R - 1 - r], c.extra[P + r * NB], v[1 + 2 * r],
+                         v[1 + 2 * (R - 1 - r)]);
+            }
+        }
+    }
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        const float2 zero = make_float2(0.0f, 0.0f);
+        if (!c.active) {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = zero;
+            }
+            return;
+        }
+        const float2* row = x + c.tf * keep;
+        const int kp = keep;
+        prepare<PL>(v, c, [&](int k) { return k < kp ? __ldg(row + k) : zero; });
+    }
+
+    template <class PL>
+    __host__ __device__ static constexpr int staged_input_entries() { return PL::G * (PL::N + 1) + 2; }
+    template <class PL>
+    __device__ __forceinline__ void stage_src(long long tf0, int count, const float2*& src,
+                                              unsigned& bytes, int& shift) const
+    {
+        C2rIo{x, y, keep, scale}.template stage_src<PL>(tf0, count, src, bytes, shift);
+    }
+    template <class PL>
+    __device__ __forceinline__ void load_staged(float2 (&v)[PL::E], const RowCtx& c,
+                                                const float2* tile) const
+    {
+        const float2 zero = make_float2(0.0f, 0.0f);
+        if (!c.active) {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = zero;
+            }
+            return;
+        }
+        const float2* row = tile + c.g * keep;
+        const int kp = keep;
+        prepare<PL>(v, c, [&](int k) { return k < kp ? row[k] : zero; });
+    }
+
+    template <class PL, bool Inv>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        C2rIo{x, y, keep, scale}.template store<PL, Inv>(v, c);
     }
 };
 

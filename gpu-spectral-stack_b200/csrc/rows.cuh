@@ -34,7 +34,7 @@ void launch_rows(const Io& io, long long batch, cudaStream_t stream, const float
     auto kernel = row_kernel<PL, Inv, B, Table, Io>;
     constexpr std::size_t smem = row_smem_bytes<PL, Io>();
     static std::atomic<int> cache[kMaxDevices];
-    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E) : nullptr;
+    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E, PL::SmallLast) : nullptr;
     const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem,
                                           cache, (batch + PL::G - 1) / PL::G);
     kernel<<<grid, PL::THREADS, smem, stream>>>(io, batch, tw, extra_table);
@@ -57,7 +57,7 @@ void launch_rows_staged(const Io& io, long long batch, cudaStream_t stream, cons
     constexpr std::size_t smem = staged_smem_bytes<PL, Io>();
     static_assert(smem <= 227 * 1024, "staged tile does not fit in shared memory");
     static std::atomic<int> cache[kMaxDevices];
-    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E) : nullptr;
+    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E, PL::SmallLast) : nullptr;
     const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem,
                                           cache, (batch + PL::G - 1) / PL::G);
     kernel<<<grid, PL::THREADS, smem, stream>>>(io, batch, tw, extra_table, device_fault_word());
@@ -116,26 +116,42 @@ struct RowEngine {
     }
 
     // `batch` real rows of n points (2 <= n <= 8192) to rows of `keep` (1 .. n/2 + 1) outputs.
+    // Where the plan with the small radix last leaves two butterflies per thread in the last
+    // pass, the combine runs in registers on mirror pairs (R2cPairIo).
     static void r2c(const float* x, float2* y, int n, long long batch, int keep, float2* /*work*/,
                     cudaStream_t s)
     {
         dispatch_pow2<1, kMaxRowN>(n / 2, [&](auto m_) {
             constexpr int M = decltype(m_)::value;
-            using PL = PlanFor<M>;
             const float2* w = Table ? twiddles::half_turn(M) : nullptr;
-            const R2cIo io{reinterpret_cast<const float2*>(x), y, keep};
-            if constexpr (M >= kMinStagedN) {
-                if (aligned16(x)) {
-                    launch_rows_staged<PL, false, B, Table>(io, batch, s, w);
-                    return;
+            const auto* xz = reinterpret_cast<const float2*>(x);
+            using PP = Plan<M, default_e(M), true>;
+            if constexpr (M >= 32 && PP::kPairLast) {
+                const R2cPairIo io{xz, y, keep};
+                if constexpr (M >= kMinStagedN) {
+                    if (aligned16(x)) {
+                        launch_rows_staged<PP, false, B, Table>(io, batch, s, w);
+                        return;
+                    }
                 }
+                launch_rows<PP, false, B, Table>(io, batch, s, w);
+            } else {
+                using PL = PlanFor<M>;
+                const R2cIo io{xz, y, keep};
+                if constexpr (M >= kMinStagedN) {
+                    if (aligned16(x)) {
+                        launch_rows_staged<PL, false, B, Table>(io, batch, s, w);
+                        return;
+                    }
+                }
+                launch_rows<PL, false, B, Table>(io, batch, s, w);
             }
-            launch_rows<PL, false, B, Table>(io, batch, s, w);
         });
     }
 
     // Rows of `keep` (1 .. n/2 + 1) complex inputs, the rest zero, to real rows of n points,
-    // divided by n.
+    // divided by n. Where the first pass has two butterflies per thread, the prepare step runs
+    // in registers on mirror pairs (C2rPairIo).
     static void c2r(const float2* x, float* y, int n, long long batch, int keep, float2* /*work*/,
                     cudaStream_t s)
     {
@@ -143,16 +159,29 @@ struct RowEngine {
             constexpr int M = decltype(m_)::value;
             using PL = PlanFor<M>;
             const float2* w = Table ? twiddles::half_turn(M) : nullptr;
-            const C2rIo io{x, reinterpret_cast<float2*>(y), keep, 1.0f / M};
-            if constexpr (M >= kMinStagedN) {
-                // The copy of a tile is rounded to 16 bytes; with batch * keep even and x aligned
-                // the rounding never reaches past the end of x.
-                if (aligned16(x) && (batch * keep) % 2 == 0) {
-                    launch_rows_staged<PL, true, B, Table>(io, batch, s, w);
-                    return;
+            auto* yz = reinterpret_cast<float2*>(y);
+            // The staged copy of a tile is rounded to 16 bytes; with batch * keep even and x
+            // aligned the rounding never reaches past the end of x.
+            const bool staged = M >= kMinStagedN && aligned16(x) && (batch * keep) % 2 == 0;
+            if constexpr (M >= 32 && PL::kPairFirst) {
+                const C2rPairIo io{x, yz, keep, 1.0f / M};
+                if constexpr (M >= kMinStagedN) {
+                    if (staged) {
+                        launch_rows_staged<PL, true, B, Table>(io, batch, s, w);
+                        return;
+                    }
                 }
+                launch_rows<PL, true, B, Table>(io, batch, s, w);
+            } else {
+                const C2rIo io{x, yz, keep, 1.0f / M};
+                if constexpr (M >= kMinStagedN) {
+                    if (staged) {
+                        launch_rows_staged<PL, true, B, Table>(io, batch, s, w);
+                        return;
+                    }
+                }
+                launch_rows<PL, true, B, Table>(io, batch, s, w);
             }
-            launch_rows<PL, true, B, Table>(io, batch, s, w);
         });
     }
 };

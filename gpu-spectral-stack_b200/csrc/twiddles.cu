@@ -67,15 +67,15 @@ const float2* get(const Key& key, long long count, Build&& build)
 
 }  // namespace
 
-const float2* pass_table(int n, int e)
+const float2* pass_table(int n, int e, bool small_last)
 {
-    const int entries = engine::plan_tw_entries(n, e);
-    return get(Key{0, n, e}, entries < 1 ? 1 : entries, [&](std::vector<float2>& t) {
+    const int entries = engine::plan_tw_entries(n, e, small_last);
+    return get(Key{small_last ? 3 : 0, n, e}, entries < 1 ? 1 : entries, [&](std::vector<float2>& t) {
         const int passes = engine::plan_passes(n, e);
         for (int s = 1; s < passes; ++s) {
-            const int L = engine::plan_span(n, e, s);
-            const int R = engine::plan_radix(n, e, s);
-            const int off = engine::plan_tw_offset(n, e, s);
+            const int L = engine::plan_span(n, e, s, small_last);
+            const int R = engine::plan_radix(n, e, s, small_last);
+            const int off = engine::plan_tw_offset(n, e, s, small_last);
             for (int r = 0; r < R; ++r) {
                 for (int k = 0; k < L; ++k) {
                     t[static_cast<std::size_t>(off + r * L + k)] = forward_factor(

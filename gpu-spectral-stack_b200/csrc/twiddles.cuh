@@ -15,7 +15,7 @@ namespace spectral::twiddles {
 
 // The pass tables of plan (n, e) in the engine's layout (engine.cuh): plan_tw_entries(n, e)
 // entries; entry r L + k of pass s is W_{L R}^(k r) = exp(-2 pi i k r / (L R)).
-const float2* pass_table(int n, int e);
+const float2* pass_table(int n, int e, bool small_last = false);
 
 // W_{2n}^k = exp(-pi i k / n) for k = 0 .. n: n + 1 entries (real-transform combine).
 const float2* half_turn(int n);

@@ -3,13 +3,14 @@
 // variants compile in parallel.
 
 #include "backend.hpp"
-#include "columns.cuh"
+#include "pruned2d.cuh"
 
 namespace spectral {
 namespace {
 
 using Rows = engine::RowEngine<4, false>;
 using Cols = engine::ColumnEngine<4, false>;
+using Fused = engine::Pruned2dEngine<4, false>;
 
 void c2c(const float2* x, float2* y, int n, long long batch, Direction d, int keep, cudaStream_t s)
 {
@@ -22,6 +23,7 @@ void c2c(const float2* x, float2* y, int n, long long batch, Direction d, int ke
 
 }  // namespace
 
-const Backend kEngineR4 = {&c2c, &Rows::r2c, &Rows::c2r, &Cols::columns};
+const Backend kEngineR4 = {&c2c, &Rows::r2c, &Rows::c2r, &Cols::columns, &Fused::supported,
+                      &Fused::forward, &Fused::inverse};
 
 }  // namespace spectral

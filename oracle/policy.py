@@ -9,6 +9,13 @@ A restatement of the reference's python/spectral/testing.py with the limit tight
 dominate, and it is checked per transform so one bad transform cannot hide in a batch. Round
 trips get twice the limit, as in the reference's tests (test_fft.py:57). A wrong index, twiddle
 or race gives errors of order 1, far above any of these limits.
+
+Truncated outputs (fft_truncated, rfft2_truncated) keep a few modes of a transform. Their
+absolute error is that of the full transform, but a handful of kept modes of a random input can
+be arbitrarily small (one kept mode is a sum that may cancel), so dividing by their own norm
+measures the input's cancellation rather than the transform. assert_truncated_close therefore
+divides by the norm the kept modes have on average: the full transform's norm scaled by
+sqrt(kept / total).
 """
 
 from __future__ import annotations
@@ -53,6 +60,31 @@ def assert_transform_close(
     worst error."""
     tol = fft_tolerance(n) if tol is None else tol
     err = relative_error(actual, expected, axes)
+    worst = float(np.max(err)) if np.size(err) else 0.0
+    if worst > tol:
+        where = np.unravel_index(int(np.argmax(err)), np.shape(err)) if np.ndim(err) else ()
+        raise AssertionError(
+            f"relative L2 error {worst:.3e} exceeds the tolerance {tol:.3e} "
+            f"(n = {n}) in transform {tuple(int(i) for i in where)}"
+        )
+    return worst
+
+
+def assert_truncated_close(
+    actual, expected, full, n: int, axes: tuple[int, ...] = (-1,), tol: float | None = None
+) -> float:
+    """Like assert_transform_close for the kept modes `expected` of the full transform `full`."""
+    tol = fft_tolerance(n) if tol is None else tol
+    a = to_numpy(actual).astype(np.complex128)
+    e = to_numpy(expected).astype(np.complex128)
+    f = to_numpy(full).astype(np.complex128)
+    if a.shape != e.shape:
+        raise AssertionError(f"shape {a.shape} differs from the expected {e.shape}")
+    kept = np.prod([e.shape[ax] for ax in axes])
+    total = np.prod([f.shape[ax] for ax in axes])
+    num = np.sqrt(np.sum(np.abs(a - e) ** 2, axis=axes))
+    den = np.sqrt(np.sum(np.abs(f) ** 2, axis=axes) * (kept / total))
+    err = num / np.maximum(den, np.finfo(np.float64).tiny)
     worst = float(np.max(err)) if np.size(err) else 0.0
     if worst > tol:
         where = np.unravel_index(int(np.argmax(err)), np.shape(err)) if np.ndim(err) else ()

@@ -172,6 +172,20 @@ def test_policy_rejects_one_bad_transform_in_a_batch(rng):
         policy.assert_transform_close(actual, exact, n)
 
 
+def test_truncated_policy_scales_by_the_full_transform(rng):
+    # One kept mode that cancels to almost nothing: its own norm would make a rounding-level
+    # error look huge; against the full transform's scale it is rounding-level.
+    n = 8
+    x = policy.random_complex(rng, (1, n)).astype(np.complex128)
+    x[0, -1] -= x.sum()  # X[0] = sum(x) = 0
+    full = ref.fft(x)
+    kept = full[:, :1]
+    noisy = kept + 1e-8
+    with pytest.raises(AssertionError):
+        policy.assert_transform_close(noisy, kept, n)
+    policy.assert_truncated_close(noisy, kept, full, n)
+
+
 def test_policy_limit_is_two_eps_per_stage():
     assert policy.fft_tolerance(4096) == pytest.approx(2 * policy.FLOAT32_EPS * 12)
     assert policy.fft_tolerance(2) == pytest.approx(2 * policy.FLOAT32_EPS)

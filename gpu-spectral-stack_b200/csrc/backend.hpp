@@ -51,4 +51,10 @@ extern const Backend kNaive;
 // Records the calling thread's error message for spectral_last_error() (capi.cu).
 void set_last_error(const std::string& message);
 
+// The strided-column complex-to-real 2D transform with a caller-given workspace of
+// `work_values` complex values, checked and run as spectral_fft2_c2r does (capi.cu); returns a
+// status code.
+int run_fft2_c2r_strided(const char* impl, const void* x, float* y, int n1, int n2,
+                         long long batch, float2* work, std::size_t work_values, void* stream);
+
 }  // namespace spectral

@@ -339,6 +339,22 @@ std::size_t irfft2_modes_work(const Impl& impl, int n1, int n2, int m1, int m2, 
 
 void set_last_error(const std::string& message) { g_last_error = message; }
 
+int run_fft2_c2r_strided(const char* impl, const void* x, float* y, int n1, int n2,
+                         long long batch, float2* work, std::size_t work_values, void* stream)
+{
+    return guarded([&] {
+        const Impl& i = find(impl);
+        need(i.has_columns(), std::string(impl) + " has no strided column kernel");
+        check_2d(i, Columns::Strided, n1, n2, batch, true);
+        const std::size_t needed = fft2_c2r_work(i, Columns::Strided, n1, n2, batch);
+        need(needed <= work_values, "fft2_c2r: needs " + str(static_cast<long long>(needed))
+                                        + " complex values of scratch, more than the "
+                                        + str(static_cast<long long>(work_values)) + " available");
+        fft2_c2r(i, Columns::Strided, static_cast<const float2*>(x), y, n1, n2, batch, work,
+                 as_stream(stream));
+    });
+}
+
 }  // namespace spectral
 
 using namespace spectral;

@@ -51,6 +51,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_fft2_c2c": (_i, [_s, _i, _p, _p, _i, _i, _ll, _i, _p, _p]),
     "spectral_fft2_r2c": (_i, [_s, _i, _p, _p, _i, _i, _ll, _p, _p]),
     "spectral_fft2_c2r": (_i, [_s, _i, _p, _p, _i, _i, _ll, _p, _p]),
+    "spectral_fft2_c2r_noalloc": (_i, [_s, _p, _p, _i, _i, _ll, _p]),
     "spectral_c2c_pruned_workspace": (_i, [_s, _i, _i, _ll, _szp]),
     "spectral_c2c_pruned": (_i, [_s, _p, _p, _i, _i, _ll, _i, _p, _p]),
     "spectral_rfft2_modes_workspace": (_i, [_s, _i, _i, _i, _i, _ll, _szp]),

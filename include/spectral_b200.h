@@ -120,6 +120,21 @@ SPECTRAL_API int spectral_fft2_r2c(const char* impl, int columns, const float* x
 SPECTRAL_API int spectral_fft2_c2r(const char* impl, int columns, const void* x, float* y, int n1, int n2,
                       long long batch, void* work, void* stream);
 
+/* The complex-to-real 2D transform (strided columns) without any allocation, for callers that
+ * cannot allocate device memory: a plugin whose host framework owns every allocation, a
+ * real-time loop that must stay out of the CUDA allocator, or a binding that has device pointers
+ * but no allocator. Its workspace is a fixed array inside the library of
+ * SPECTRAL_NOALLOC_SCRATCH_VALUES complex values (32 MiB), held on every GPU that loads the
+ * library until the process exits; larger transforms (batch * n1 * (n2/2 + 1) values) are
+ * rejected with SPECTRAL_INVALID_ARGUMENT. All calls on a device share that array, so calls that
+ * overlap on the GPU race and must be serialised by the caller. The first call on each device
+ * looks up the array's device address; make it before any stream capture. Results equal
+ * spectral_fft2_c2r with SPECTRAL_COLUMNS_STRIDED. No counterpart in the reference, which always
+ * allocates its workspaces. */
+#define SPECTRAL_NOALLOC_SCRATCH_VALUES (1u << 22)
+SPECTRAL_API int spectral_fft2_c2r_noalloc(const char* impl, const void* x, float* y, int n1, int n2,
+                                           long long batch, void* stream);
+
 /* --- pruned, the FNO transforms (reference: csrc/fft/pruned.hpp:26-43) ------------------------ */
 
 SPECTRAL_API int spectral_c2c_pruned_workspace(const char* impl, int n, int keep, long long batch, size_t* count);

@@ -184,11 +184,17 @@ __device__ __forceinline__ void dft4(float2 (&v)[4])
     const float2 d02 = csub(v[0], v[2]);
     const float2 s13 = cadd(v[1], v[3]);
     const float2 d13 = csub(v[1], v[3]);
-    const float2 rot = mul_w<1, 4, Inv>(d13);  // -i (forward) or +i (inverse) times (b - d)
     v[0] = cadd(s02, s13);
     v[2] = csub(s02, s13);
-    v[1] = cadd(d02, rot);
-    v[3] = csub(d02, rot);
+    // d02 -+ i d13: the rotation swaps real and imaginary parts, so it stays scalar (a packed
+    // operand would need the swapped pair built first).
+    if constexpr (Inv) {
+        v[1] = make_float2(d02.x - d13.y, d02.y + d13.x);
+        v[3] = make_float2(d02.x + d13.y, d02.y - d13.x);
+    } else {
+        v[1] = make_float2(d02.x + d13.y, d02.y - d13.x);
+        v[3] = make_float2(d02.x - d13.y, d02.y + d13.x);
+    }
 }
 
 template <int R, int B, bool Inv>

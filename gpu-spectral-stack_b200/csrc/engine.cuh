@@ -83,7 +83,7 @@ __host__ __device__ constexpr int plan_tw_entries(int n, int e, bool small_last 
     return plan_tw_offset(n, e, plan_passes(n, e), small_last);
 }
 
-template <int N_, int E_, bool SmallLast_ = false>
+template <int N_, int E_, bool SmallLast_ = false, int MinThreads_ = kMinThreads>
 struct Plan {
     static constexpr int N = N_;
     static constexpr int E = E_;
@@ -91,7 +91,7 @@ struct Plan {
     static_assert(is_pow2(N) && is_pow2(E) && E <= N && E <= 32 && (N == 1 || E >= 2), "bad plan");
     static constexpr int P = N / E;  // threads per transform
     static constexpr int PASSES = plan_passes(N, E);
-    static constexpr int THREADS = cmax(kMinThreads, P);
+    static constexpr int THREADS = cmax(MinThreads_, P);  // a CTA holds G = THREADS / P transforms
     static constexpr int G = THREADS / P;  // transforms per CTA
 
     __host__ __device__ static constexpr int radix(int s) { return plan_radix(N, E, s, SmallLast); }

@@ -22,8 +22,26 @@ __host__ __device__ constexpr int default_e(int n)
     return n <= 16 ? n : n <= 64 ? 8 : n <= 256 ? 16 : n <= 1024 ? 32 : n <= 8192 ? 16 : 32;
 }
 
+// Threads per CTA (the CTA holds THREADS / P transforms). Measured on B200 at 2^24 points per
+// call: for 1024 and 2048 points, 128-thread CTAs (4 and 1 transforms) leave more CTAs per SM
+// than 256-thread ones, whose twiddle tables and buffers fill shared memory; that beats larger
+// CTAs by 7-10 %.
+__host__ __device__ constexpr int default_threads(int n)
+{
+    return (n == 1024 || n == 2048) ? 128 : kMinThreads;
+}
+
 template <int N>
-using PlanFor = Plan<N, default_e(N)>;
+using PlanFor = Plan<N, default_e(N), false, default_threads(N)>;
+
+// The plan with the small radix last, for the mirror-paired real-to-complex rows.
+template <int N>
+using PlanR2c = Plan<N, default_e(N), true, default_threads(N)>;
+
+// Complex rows: the bulk-copy prefetch pays where a transform spans several warps; for 1024
+// points (one warp per transform, 4 CTAs of 4 transforms per SM) direct loads measured 10 %
+// faster than the staged kernel, whose second buffer halves the CTAs that fit.
+__host__ __device__ constexpr bool stage_c2c(int n) { return n >= 2048; }
 
 template <class PL, bool Inv, int B, bool Table, class Io>
 void launch_rows(const Io& io, long long batch, cudaStream_t stream, const float2* extra_table)
@@ -92,10 +110,10 @@ struct RowEngine {
         dispatch_pow2<2, kMaxRowN>(n, [&](auto n_) {
             constexpr int N = decltype(n_)::value;
             using PL = PlanFor<N>;
-            const bool staged = N >= kMinStagedN && aligned16(x);
+            const bool staged = stage_c2c(N) && aligned16(x);
             if (d == Direction::Forward) {
                 const C2cIo io{x, y, N, keep, 1.0f};
-                if constexpr (N >= kMinStagedN) {
+                if constexpr (stage_c2c(N)) {
                     if (staged) {
                         launch_rows_staged<PL, false, B, Table>(io, batch, s, nullptr);
                         return;
@@ -104,7 +122,7 @@ struct RowEngine {
                 launch_rows<PL, false, B, Table>(io, batch, s, nullptr);
             } else {
                 const C2cIo io{x, y, keep, N, 1.0f / N};
-                if constexpr (N >= kMinStagedN) {
+                if constexpr (stage_c2c(N)) {
                     if (staged && keep == N) {
                         launch_rows_staged<PL, true, B, Table>(io, batch, s, nullptr);
                         return;
@@ -125,7 +143,7 @@ struct RowEngine {
             constexpr int M = decltype(m_)::value;
             const float2* w = Table ? twiddles::half_turn(M) : nullptr;
             const auto* xz = reinterpret_cast<const float2*>(x);
-            using PP = Plan<M, default_e(M), true>;
+            using PP = PlanR2c<M>;
             if constexpr (M >= 32 && PP::kPairLast) {
                 const R2cPairIo io{xz, y, keep};
                 if constexpr (M >= kMinStagedN) {

@@ -1,0 +1,320 @@
+// The large single-field 2D complex FFT, slab-decomposed by rows over R ranks (one per GPU).
+// The reference has no counterpart: its fft2 stops at 4096 points per side
+// (csrc/fft/fft2d.cu:65-75) and it has no multi-GPU code.
+//
+// An n x n field; rank r holds rows [r n/R, (r+1) n/R) ("rows" of them), w = n / R.
+//
+//   forward   1. spectral_slab_rows: n-point row transforms of the local rows, each stored into R
+//               contiguous chunks, chunk s = columns [s w, (s+1) w) of every local row: the
+//               send buffer of an all-to-all, [s][row][c].
+//             2. all-to-all (the caller's NCCL; spectral.distributed uses torch.distributed):
+//               rank s receives [r][row][c] from every r, which is exactly the n x w row-major
+//               matrix of the field's columns [s w, (s+1) w).
+//             3. spectral_slab_columns: n-point transforms down those w columns, natural order.
+//   inverse   the same steps backwards: columns on the column slab (its row blocks are the send
+//             chunks), the all-to-all, then row transforms whose input is gathered from the R
+//             received chunks.
+//
+// Rows of up to 16384 points are transformed on chip in one pass; their larger twiddle tables
+// are read from the correctly rounded table in global memory (L2-resident) instead of being
+// copied to shared memory, which then holds only the transform. Columns longer than 4096 points
+// use two column-tile passes (four-step, n = n1 n2): the first in place with the inter-pass
+// twiddles, the second into the output in natural order. Every global access is a run of at
+// least 16 consecutive complex values.
+
+#include "../../include/spectral_b200.h"
+
+#include "backend.hpp"
+#include "columns.cuh"
+
+#include <climits>
+
+namespace spectral {
+namespace {
+
+using namespace engine;
+
+constexpr int kMaxSlabN = 16384;
+
+template <int N>
+using SlabPlan = Plan<N, (N <= 4096 ? default_e(N) : N == 8192 ? 16 : 32), false,
+                      (N <= 4096 ? default_threads(N) : kMinThreads)>;
+
+// Rows of a slab: contiguous rows on the natural side, R chunks of w columns on the chunked side
+// (element (row, k) at chunk k / w, offset row * w + k % w). Forward reads natural and writes
+// chunked; inverse reads chunked and writes natural.
+template <bool Inv>
+struct SlabRowIo {
+    const float2* x;
+    float2* y;
+    long long rows;  // rows per rank
+    int wlog;        // log2 of the columns per chunk
+    float scale;
+
+    __device__ __forceinline__ long long chunked(long long row, int k) const
+    {
+        const int s = k >> wlog;
+        return ((static_cast<long long>(s) * rows + row) << wlog) + (k & ((1 << wlog) - 1));
+    }
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], long long row, int t) const
+    {
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const int k = t + i * PL::P;
+            v[i] = Inv ? x[chunked(row, k)] : x[row * PL::N + k];
+        }
+    }
+
+    template <class PL>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], long long row, int t) const
+    {
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const int k = t + i * PL::P;
+            if constexpr (Inv) {
+                y[row * PL::N + k] = cscale(v[i], scale);
+            } else {
+                y[chunked(row, k)] = v[i];
+            }
+        }
+    }
+};
+
+template <class PL, bool Inv>
+__global__ void __launch_bounds__(PL::THREADS)
+    slab_row_kernel(const SlabRowIo<Inv> io, const float2* __restrict__ tw)
+{
+    extern __shared__ float4 smem_raw[];
+    float2* bufs = reinterpret_cast<float2*>(smem_raw);
+    const int g = threadIdx.x / PL::P;
+    const int t = threadIdx.x - g * PL::P;
+    float2* buf = bufs + g * PL::BUF;
+    for (long long r0 = static_cast<long long>(blockIdx.x) * PL::G; r0 < io.rows;
+         r0 += static_cast<long long>(gridDim.x) * PL::G) {
+        const long long row = r0 + g;
+        const bool active = row < io.rows;
+        float2 v[PL::E];
+        if (active) {
+            io.template load<PL>(v, row, t);
+        } else {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = make_float2(0.0f, 0.0f);
+            }
+        }
+        run_passes<PL, Inv, 8>(v, t, buf, tw);  // twiddles straight from the global table
+        if (active) {
+            io.template store<PL>(v, row, t);
+        }
+    }
+}
+
+template <bool Inv>
+void slab_rows(const float2* x, float2* y, int n, long long rows, int ranks, cudaStream_t s)
+{
+    dispatch_pow2<2, kMaxSlabN>(n, [&](auto n_) {
+        constexpr int N = decltype(n_)::value;
+        using PL = SlabPlan<N>;
+        const SlabRowIo<Inv> io{x, y, rows, ilog2(n / ranks), Inv ? 1.0f / N : 1.0f};
+        auto kernel = slab_row_kernel<PL, Inv>;
+        constexpr std::size_t smem = sizeof(float2) * static_cast<std::size_t>(PL::G) * PL::BUF;
+        static std::atomic<int> cache[kMaxDevices];
+        const float2* tw = twiddles::pass_table(PL::N, PL::E);
+        const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS,
+                                              smem, cache, (rows + PL::G - 1) / PL::G);
+        kernel<<<grid, PL::THREADS, smem, s>>>(io, tw);
+        SPECTRAL_CUDA(cudaGetLastError());
+    });
+}
+
+// Pass 1 of an n = n1 n2 column transform over an n x w row-major matrix (four-step, Bailey):
+// transform f = n2 w + c is column c at rows p n2 + n2 (an n1-point transform); its output k1 is
+// multiplied by W_n^(k1 n2) and stored in place, at row k1 n2 + n2.
+struct SlabColumnPass1Io {
+    float2* x;
+    int w;
+    int n2;
+    int n;
+    float scale;  // 1 / n1 for the inverse
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], const ColumnCtx& c) const
+    {
+        if (!c.active) {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = make_float2(0.0f, 0.0f);
+            }
+            return;
+        }
+        const float2* b = x + c.f;  // column c of row n2 is element n2 w + c = f
+        const long long stride = static_cast<long long>(n2) * w;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            v[i] = b[(c.t + i * PL::P) * stride];
+        }
+    }
+
+    template <class PL, int C, bool Inv>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], const ColumnCtx& c) const
+    {
+        if (!c.active) {
+            return;
+        }
+        const int q = static_cast<int>(c.f / w);
+        float2* b = x + c.f;
+        const long long stride = static_cast<long long>(n2) * w;
+        const float step = 2.0f / static_cast<float>(n);  // exact: n is a power of two
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const int k1 = c.t + i * PL::P;
+            float sn = 0.0f;
+            float cs = 1.0f;
+            sincospif(static_cast<float>(k1 * q) * step, &sn, &cs);  // k1 q < n <= 2^14: exact
+            const float2 r = cmul_tw<Inv>(v[i], make_float2(cs, -sn));
+            b[k1 * stride] = Inv ? cscale(r, scale) : r;
+        }
+    }
+};
+
+// Pass 2: transform f = k1 w + c is column c at rows k1 n2 + p (an n2-point transform); its output
+// k2 is X[k1 + n1 k2], stored into y at that row.
+struct SlabColumnPass2Io {
+    const float2* x;
+    float2* y;
+    int w;
+    int n1;
+    int n2;
+    float scale;  // 1 / n2 for the inverse
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], const ColumnCtx& c) const
+    {
+        if (!c.active) {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = make_float2(0.0f, 0.0f);
+            }
+            return;
+        }
+        const long long k1 = c.f / w;
+        const long long col = c.f - k1 * w;
+        const float2* b = x + (k1 * n2) * w + col;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            v[i] = b[static_cast<long long>(c.t + i * PL::P) * w];
+        }
+    }
+
+    template <class PL, int C, bool Inv>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], const ColumnCtx& c) const
+    {
+        if (!c.active) {
+            return;
+        }
+        const long long k1 = c.f / w;
+        const long long col = c.f - k1 * w;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const long long k2 = c.t + i * PL::P;
+            y[(k1 + static_cast<long long>(n1) * k2) * w + col] = Inv ? cscale(v[i], scale) : v[i];
+        }
+    }
+};
+
+template <bool Inv>
+void slab_columns(float2* x, float2* y, int n, int w, cudaStream_t s)
+{
+    if (n <= kMaxRowN) {
+        kEngineR8.columns(x, y, n, w, 1, 0, 0, Inv ? Direction::Inverse : Direction::Forward, s);
+        return;
+    }
+    const int n1 = 1 << (ilog2(n) / 2);
+    const int n2 = n / n1;
+    dispatch_pow2<2, kMaxRowN>(n1, [&](auto n1_) {
+        constexpr int N1 = decltype(n1_)::value;
+        launch_columns<PlanFor<N1>, Inv, 8, false>(
+            SlabColumnPass1Io{x, w, n2, n, Inv ? 1.0f / N1 : 1.0f},
+            static_cast<long long>(n2) * w, s);
+    });
+    dispatch_pow2<2, kMaxRowN>(n2, [&](auto n2_) {
+        constexpr int N2 = decltype(n2_)::value;
+        launch_columns<PlanFor<N2>, Inv, 8, false>(
+            SlabColumnPass2Io{x, y, w, n1, n2, Inv ? 1.0f / N2 : 1.0f},
+            static_cast<long long>(n1) * w, s);
+    });
+}
+
+void check_slab(int n, int ranks)
+{
+    if (!is_pow2(n) || n < 2 || n > kMaxSlabN) {
+        throw InvalidArgument("fft2_slab: n must be a power of two from 2 to "
+                              + std::to_string(kMaxSlabN) + ", got " + std::to_string(n));
+    }
+    if (ranks < 1 || !is_pow2(ranks) || ranks > n) {
+        throw InvalidArgument("fft2_slab: the ranks (" + std::to_string(ranks)
+                              + ") must be a power of two dividing n = " + std::to_string(n));
+    }
+}
+
+template <class F>
+int slab_guarded(F&& f)
+{
+    try {
+        f();
+        return SPECTRAL_OK;
+    } catch (const InvalidArgument& e) {
+        set_last_error(e.what());
+        return SPECTRAL_INVALID_ARGUMENT;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return SPECTRAL_CUDA_ERROR;
+    }
+}
+
+}  // namespace
+}  // namespace spectral
+
+extern "C" int spectral_slab_rows(const void* x, void* y, int n, long long rows, int ranks,
+                                  int inverse, void* stream)
+{
+    using namespace spectral;
+    return slab_guarded([&] {
+        check_slab(n, ranks);
+        if (rows < 1 || rows > INT_MAX) {
+            throw InvalidArgument("fft2_slab: rows must be from 1 to INT_MAX");
+        }
+        const auto* xs = static_cast<const float2*>(x);
+        auto* ys = static_cast<float2*>(y);
+        const auto s = static_cast<cudaStream_t>(stream);
+        if (inverse) {
+            slab_rows<true>(xs, ys, n, rows, ranks, s);
+        } else {
+            slab_rows<false>(xs, ys, n, rows, ranks, s);
+        }
+    });
+}
+
+extern "C" int spectral_slab_columns(void* x, void* y, int n, int width, int inverse, void* stream)
+{
+    using namespace spectral;
+    return slab_guarded([&] {
+        check_slab(n, 1);
+        if (width < 1) {
+            throw InvalidArgument("fft2_slab: width must be at least 1");
+        }
+        if (x == y) {
+            throw InvalidArgument("fft2_slab: columns are transformed out of place (x != y)");
+        }
+        auto* xs = static_cast<float2*>(x);
+        auto* ys = static_cast<float2*>(y);
+        const auto s = static_cast<cudaStream_t>(stream);
+        if (inverse) {
+            slab_columns<true>(xs, ys, n, width, s);
+        } else {
+            slab_columns<false>(xs, ys, n, width, s);
+        }
+    });
+}

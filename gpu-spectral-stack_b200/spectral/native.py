@@ -58,6 +58,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_irfft2_modes_workspace": (_i, [_s, _i, _i, _i, _i, _ll, _szp]),
     "spectral_rfft2_modes": (_i, [_s, _p, _p, _i, _i, _i, _i, _ll, _p, _p]),
     "spectral_irfft2_modes": (_i, [_s, _p, _p, _i, _i, _i, _i, _ll, _p, _p]),
+    "spectral_slab_rows": (_i, [_p, _p, _i, _ll, _i, _i, _p]),
+    "spectral_slab_columns": (_i, [_p, _p, _i, _i, _i, _p]),
     "spectral_mode_contract": (_i, [_p, _p, _p, _ll, _i, _i, _ll, _p]),
 }
 

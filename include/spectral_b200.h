@@ -155,6 +155,22 @@ SPECTRAL_API int spectral_rfft2_modes(const char* impl, const float* x, void* mo
 SPECTRAL_API int spectral_irfft2_modes(const char* impl, const void* modes, float* y, int n1, int n2, int m1,
                           int m2, long long batch, void* work, void* stream);
 
+/* --- the large single-field 2D transform, slab-decomposed over ranks --------------------------- */
+/* An n x n complex field (n a power of two up to 16384) whose rows are split over `ranks` GPUs
+ * (rank r holds rows r n/ranks ..), w = n / ranks. No counterpart in the reference: its fft2
+ * stops at 4096 per side (csrc/fft/fft2d.cu:65-75) and it has no multi-GPU code.
+ * Forward: spectral_slab_rows(x = the rank's rows x n, y = `ranks` chunks [s][row][c] of w
+ * columns each), an all-to-all of those chunks (caller's NCCL), then spectral_slab_columns on
+ * the received n x w matrix: the rank's w columns of the 2D transform, natural order.
+ * Inverse (divided by n^2 overall): spectral_slab_columns(inverse) on the column slab, the
+ * all-to-all of its row blocks, then spectral_slab_rows(inverse) from the received chunks. */
+SPECTRAL_API int spectral_slab_rows(const void* x, void* y, int n, long long rows, int ranks,
+                                    int inverse, void* stream);
+/* n-point transforms down every column of the n x width row-major matrix x, into y (natural
+ * order, same layout). x is used as scratch for n > 4096 and must not be y. */
+SPECTRAL_API int spectral_slab_columns(void* x, void* y, int n, int width, int inverse,
+                                       void* stream);
+
 /* --- per-mode channel contraction of an FNO spectral convolution --------------------------- */
 
 /* out[b, o, m] = sum_i x[b, i, m] * w[i, o, m] over complex values: x (batch, cin, modes),

@@ -1,0 +1,75 @@
+"""The slab decomposition of the large 2D transform on CPU ranks (gloo): the chunk layout, the
+all-to-all and the column slab, with numpy stand-ins for the kernels (whose layouts the GPU
+tests in test_slab.py check). world_size 2 and 4, spawned processes."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+N = 32
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def field() -> np.ndarray:
+    rng = np.random.default_rng(5)
+    return (rng.standard_normal((N, N)) + 1j * rng.standard_normal((N, N))).astype(np.complex64)
+
+
+def rows_stub(x, n, rows, ranks, inverse):
+    a = x.numpy().astype(np.complex128)
+    if not inverse:
+        y = np.fft.fft(a, axis=1).reshape(rows, ranks, n // ranks).transpose(1, 0, 2)
+    else:
+        y = np.fft.ifft(a.transpose(1, 0, 2).reshape(rows, n), axis=1)
+    return torch.from_numpy(np.ascontiguousarray(y).astype(np.complex64))
+
+
+def columns_stub(x, n, width, inverse):
+    a = x.numpy().astype(np.complex128)
+    y = np.fft.ifft(a, axis=0) if inverse else np.fft.fft(a, axis=0)
+    return torch.from_numpy(y.astype(np.complex64))
+
+
+def worker(rank: int, world: int, port: int, out: dict) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+
+        sys.path.insert(0, os.path.join(os.path.dirname(__file__), "..", "gpu-spectral-stack_b200"))
+        from spectral.distributed import fft2_slab
+
+        rows = N // world
+        x = torch.from_numpy(field()[rank * rows:(rank + 1) * rows])
+        cols = fft2_slab(x, rows_fn=rows_stub, columns_fn=columns_stub)
+        gathered = [torch.empty_like(cols) for _ in range(world)]
+        dist.all_gather(gathered, cols)
+        back = fft2_slab(cols, inverse=True, rows_fn=rows_stub, columns_fn=columns_stub)
+        every = [torch.empty_like(back) for _ in range(world)]
+        dist.all_gather(every, back)
+        if rank == 0:
+            out["forward"] = torch.cat(gathered, dim=1).numpy()
+            out["inverse"] = torch.cat(every, dim=0).numpy()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_slab_decomposition_on_gloo_ranks(world):
+    manager = mp.get_context("spawn").Manager()
+    out = manager.dict()
+    mp.start_processes(worker, args=(world, free_port(), out), nprocs=world, start_method="spawn")
+    expected = np.fft.fft2(field().astype(np.complex128))
+    np.testing.assert_allclose(out["forward"], expected, rtol=0, atol=1e-4 * np.abs(expected).max())
+    np.testing.assert_allclose(out["inverse"], field(), rtol=0, atol=1e-5)

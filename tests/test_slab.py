@@ -1,0 +1,74 @@
+"""The slab-decomposed 2D transform's kernels on one GPU, with R ranks emulated: every "rank"
+runs spectral_slab_rows on its rows, the all-to-all is a gather done with torch, and every rank
+runs spectral_slab_columns on what it received. Checked against the float64 oracle: fully for
+small fields, on sampled output columns for the 16384 x 16384 field of the benchmark (a float64
+matrix-vector product per sampled column, then a 1D FFT)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.policy import FLOAT32_EPS, assert_transform_close, fft_tolerance
+from spectral.distributed import columns_kernel, rows_kernel
+
+pytestmark = pytest.mark.gpu
+
+
+def forward_emulated(x: torch.Tensor, ranks: int) -> list[torch.Tensor]:
+    n = x.shape[0]
+    rows = n // ranks
+    chunks = [rows_kernel(x[r * rows:(r + 1) * rows].contiguous(), n, rows, ranks, False)
+              for r in range(ranks)]
+    out = []
+    for s in range(ranks):
+        received = torch.stack([chunks[r][s] for r in range(ranks)])  # (ranks, rows, w)
+        out.append(columns_kernel(received.reshape(n, n // ranks), n, n // ranks, False))
+    return out
+
+
+def inverse_emulated(cols: list[torch.Tensor], ranks: int) -> list[torch.Tensor]:
+    n = cols[0].shape[0]
+    rows = n // ranks
+    done = [columns_kernel(c.clone(), n, n // ranks, True) for c in cols]
+    return [rows_kernel(torch.stack([done[s][r * rows:(r + 1) * rows] for s in range(ranks)]),
+                        n, rows, ranks, True) for r in range(ranks)]
+
+
+@pytest.mark.parametrize("ranks", [1, 2, 4])
+@pytest.mark.parametrize("n", [256, 1024, 8192])
+def test_slab_forward_and_inverse_match_the_oracle(rng, n, ranks):
+    if n == 8192 and ranks == 4:
+        pytest.skip("covered by the smaller cases and the 16384 case")
+    x = (rng.standard_normal((n, n)) + 1j * rng.standard_normal((n, n))).astype(np.complex64)
+    xd = torch.from_numpy(x).cuda()
+    cols = forward_emulated(xd, ranks)
+    full = torch.cat(cols, dim=1).cpu().numpy()
+    expected = np.fft.fft2(x.astype(np.complex128))
+    # One 2D transform: the whole field is a single transform of n * n points.
+    assert_transform_close(full[None], expected[None], n * n, axes=(-2, -1))
+    back = torch.cat(inverse_emulated(cols, ranks), dim=0)
+    assert_transform_close(back.cpu().numpy()[None], x[None], n * n, axes=(-2, -1),
+                           tol=2 * fft_tolerance(n * n))
+
+
+def test_benchmark_field_on_eight_ranks_sampled():
+    # 16384 x 16384, N(0,1) real and imaginary parts, 8 ranks of 2048 rows.
+    n, ranks = 16384, 8
+    g = torch.Generator(device="cuda").manual_seed(4)
+    xd = torch.complex(torch.randn(n, n, device="cuda", generator=g),
+                       torch.randn(n, n, device="cuda", generator=g))
+    cols = forward_emulated(xd, ranks)
+    x = xd.cpu().numpy()
+    w = n // ranks
+    for k2 in [0, 1, 5000, 16383]:
+        kernel = np.exp(-2j * np.pi * (np.arange(n) * k2 % n) / n)
+        expected = np.fft.fft(x.astype(np.complex128) @ kernel)     # column k2 of fft2(x)
+        got = cols[k2 // w][:, k2 % w].cpu().numpy()
+        err = np.linalg.norm(got - expected) / np.linalg.norm(expected)
+        assert err <= 2 * FLOAT32_EPS * 28, (k2, err)
+
+
+def test_rejects_bad_shapes():
+    x = torch.zeros(4, 12, dtype=torch.complex64, device="cuda")
+    with pytest.raises(ValueError, match="power of two"):
+        rows_kernel(x, 12, 4, 3, False)

@@ -221,31 +221,12 @@ std::size_t fft2_c2r_work(const Impl& impl, Columns columns, int n1, int n2, lon
     return (columns == Columns::Strided ? q : 2 * q) + real_work(impl, n1, n2, batch);
 }
 
-// The strided method runs in chunks of arrays whose intermediate fits comfortably in L2 (126 MB
-// on B200): each chunk's column pass then reads what its row pass just wrote from L2, not HBM,
-// so HBM sees roughly the input and the output once instead of two full round trips. The
-// kernels and their order per element are unchanged, so results are identical to one pass.
-constexpr std::size_t kL2ChunkBytes = 32u << 20;
-
-long long chunk_arrays(std::size_t bytes_per_array, long long batch)
-{
-    const long long c = static_cast<long long>(kL2ChunkBytes / (bytes_per_array ? bytes_per_array : 1));
-    return c < 1 ? 1 : (c > batch ? batch : c);
-}
-
 void fft2_c2c(const Impl& impl, Columns columns, const float2* x, float2* y, int n1, int n2,
               long long batch, Direction d, float2* work, cudaStream_t s)
 {
     if (columns == Columns::Strided) {
-        const std::size_t per = count3(1, n1, n2);
-        const long long chunk = chunk_arrays(per * sizeof(float2), batch);
-        for (long long b0 = 0; b0 < batch; b0 += chunk) {
-            const long long cnt = chunk < batch - b0 ? chunk : batch - b0;
-            const float2* xc = x + b0 * per;
-            float2* yc = y + b0 * per;
-            c2c_any(impl, xc, yc, n2, cnt * n1, d, n2, s);            // rows
-            columns_any(impl, yc, yc, n1, n2, cnt, 0, 0, d, s);       // columns, in place
-        }
+        c2c_any(impl, x, y, n2, batch * n1, d, n2, s);            // rows
+        columns_any(impl, y, y, n1, n2, batch, 0, 0, d, s);       // columns, in place
         return;
     }
     float2* a = work;
@@ -261,15 +242,8 @@ void fft2_r2c(const Impl& impl, Columns columns, const float* x, float2* y, int 
 {
     const int w = n2 / 2 + 1;
     if (columns == Columns::Strided) {
-        const std::size_t per_in = count3(1, n1, n2);
-        const std::size_t per_out = count3(1, n1, w);
-        const long long chunk = chunk_arrays(per_out * sizeof(float2), batch);
-        for (long long b0 = 0; b0 < batch; b0 += chunk) {
-            const long long cnt = chunk < batch - b0 ? chunk : batch - b0;
-            float2* yc = y + b0 * per_out;
-            impl.backend->r2c(x + b0 * per_in, yc, n2, cnt * n1, w, work, s);
-            columns_any(impl, yc, yc, n1, w, cnt, 0, 0, Direction::Forward, s);
-        }
+        impl.backend->r2c(x, y, n2, batch * n1, w, work, s);
+        columns_any(impl, y, y, n1, w, batch, 0, 0, Direction::Forward, s);
         return;
     }
     float2* a = work;
@@ -288,15 +262,9 @@ void fft2_c2r(const Impl& impl, Columns columns, const float2* x, float* y, int 
     const std::size_t q = count3(batch, n1, w);
     if (columns == Columns::Strided) {
         // Columns first, out of place (the input is not ours to overwrite), then rows.
-        const std::size_t per_in = count3(1, n1, w);
-        const std::size_t per_out = count3(1, n1, n2);
-        const long long chunk = chunk_arrays(per_in * sizeof(float2), batch);
-        for (long long b0 = 0; b0 < batch; b0 += chunk) {
-            const long long cnt = chunk < batch - b0 ? chunk : batch - b0;
-            float2* a = work + b0 * per_in;
-            columns_any(impl, x + b0 * per_in, a, n1, w, cnt, 0, 0, Direction::Inverse, s);
-            impl.backend->c2r(a, y + b0 * per_out, n2, cnt * n1, w, work + q + b0 * count3(1, n1, n2 / 2), s);
-        }
+        float2* a = work;
+        columns_any(impl, x, a, n1, w, batch, 0, 0, Direction::Inverse, s);
+        impl.backend->c2r(a, y, n2, batch * n1, w, work + q, s);
         return;
     }
     float2* a = work;

@@ -23,7 +23,7 @@ Also on the line: `roofline` (the dominant kernel's achieved bytes / its average
 duration against the measured HBM copy peak), `e2e` (the same metric through the public torch
 API with host buffers: pinned host -> device, both transforms, device -> host, every step),
 `cpu_baseline` (the float64 oracle, numpy's pocketfft as in the reference's CPU path, on the
-host's cores), `clocks` (nvidia-smi sampled during the timed steps) and `gpu_launches`.
+host's cores), `clocks` (SM clock and throttle reasons, sampled through NVML during the timed steps) and `gpu_launches`.
 
 --impl reference times the reference's CPU implementation of the path (the oracle port) on all
 host cores, with the same workload, metric and unit.
@@ -36,8 +36,8 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
+import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
@@ -56,7 +56,7 @@ SETS = 4
 def parse() -> argparse.Namespace:
     p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--steps", type=int, default=500)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=["real", "c2c", "rfft2", "pruned", "slab"], default="real")
@@ -451,60 +451,85 @@ def ncu_traffic(kernel: str, workload: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi sampling of one GPU's clocks and throttle reasons every 200 ms."""
+    """Samples one GPU's SM clock and clock-event (throttle) reasons through NVML, every
+    millisecond on a background thread, while the timed steps run. A timed region of a few
+    milliseconds still gets samples; nvidia-smi's -lms loop could not flush a pipe that short."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4))
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        self._handle = None
+
+    def _open(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        self._nvml = pynvml
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            self._handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+
+    def sample(self) -> None:
+        if self._handle is None:
+            return
+        n = self._nvml
+        try:
+            mhz = n.nvmlDeviceGetClockInfo(self._handle, n.NVML_CLOCK_SM)
+            reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+        except Exception:
+            return
+        self.samples.append((mhz, reasons))
+
+    def _loop(self) -> None:
+        while not self._stop.wait(0.001):
+            self.sample()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (FileNotFoundError, OSError):
-            self.proc = None
+            self._open()
+        except Exception:
+            self._handle = None
+            return self
+        self.sample()
+        self._thread = threading.Thread(target=self._loop, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+        if self._nvml is not None:
             try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
-        else:
-            self.lines = []
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self) -> dict | None:
-        if not self.lines:
+        if not self.samples:
             return None
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [v.strip() for v in ln.split(",")]
-            if len(f) < 8:
-                continue
-            try:
-                sm.append(float(f[0]))
-                mx.append(float(f[1]))
-            except ValueError:
-                continue
-            for name, val in zip(names, f[4:8]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return None
-        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [m for m, _ in self.samples]
+        reasons = set()
+        for name, const, bit in self.REASONS:
+            mask = getattr(self._nvml, const, bit)
+            if any(r & mask for _, r in self.samples):
+                reasons.add(name)
+        loaded = [m for m in sm if m > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm), "source": "NVML, 1 ms"}
 
 
 # --- CPU legs ------------------------------------------------------------------------------------

@@ -5,9 +5,10 @@
 //
 // The mode index is the fastest-varying one in all three arrays, so lane = mode: every load and
 // store of a warp is 32 consecutive complex values (256 bytes). A CTA is 32 modes by 8 warps;
-// warp w owns 8 output channels, and each thread accumulates an 8 (batch) x 8 (channel) block of
-// one mode in registers, 64 complex multiply-adds (256 FMAs) per 16 loads. x is re-read by the
-// 8 warps of a CTA through L1, w once per batch group through L2. FP32 throughout, so the
+// warp w owns 8 output channels, and each thread accumulates a 4 (batch) x 8 (channel) block of
+// one mode in registers, 32 complex multiply-adds (128 FMAs) per 12 loads. The block is sized so
+// two CTAs fit per SM (an 8 x 8 block took 204 registers and left one). x is re-read by the 8
+// warps of a CTA through L1, w once per batch group through L2. FP32 throughout, so the
 // contraction keeps the tolerance of the transforms around it.
 
 #include "../../include/spectral_b200.h"
@@ -21,10 +22,10 @@ namespace {
 
 constexpr int kModesPerCta = 32;
 constexpr int kWarps = 8;
-constexpr int kBatchPerThread = 8;
+constexpr int kBatchPerThread = 4;
 constexpr int kOutPerThread = 8;
 
-__global__ void __launch_bounds__(kModesPerCta * kWarps)
+__global__ void __launch_bounds__(kModesPerCta * kWarps, 2)
     contract_kernel(const float2* __restrict__ x, const float2* __restrict__ w,
                     float2* __restrict__ out, int batch, int cin, int cout, long long modes)
 {

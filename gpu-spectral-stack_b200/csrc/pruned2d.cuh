@@ -95,18 +95,33 @@ __global__ void __launch_bounds__(256)
                 v[i] = act ? __ldg(xf + r * M + rt + i * RP::P) : zero;
             }
             run_passes<RP, false, B>(v, rt, slot, s.twr);
+            // Combine the m2 kept outputs. Thread rt holds Z[rt + i P]; the partner Z[M - k] of
+            // k = rt + i P is register E-1-i of thread P - rt in the same warp (a row's P <= 32
+            // threads are consecutive lanes), or, for rt = 0, its own register (E - i) mod E. So
+            // a shuffle replaces staging the row's spectrum in shared memory.
+            static_assert(RP::P <= 32, "a row's threads must share a warp");
+            const int lane = threadIdx.x & 31;
+            const int partner = (lane & ~(RP::P - 1)) | ((RP::P - rt) & (RP::P - 1));
 #pragma unroll
             for (int i = 0; i < RP::E; ++i) {
-                slot[rt + i * RP::P] = v[i];
-            }
-            group_sync<RP::P>();
-            if (act) {
-                for (int k = rt; k < m2; k += RP::P) {
-                    s.colbuf[r * K::CW + k] =
-                        r2c_combine(slot[k & (M - 1)], slot[(M - k) & (M - 1)], s.half[k]);
+                if (i * RP::P >= m2) {
+                    break;  // uniform across the warp: depends on i only
+                }
+                const float2 mine = v[RP::E - 1 - i];
+                float2 zmk;
+                zmk.x = __shfl_sync(0xffffffffu, mine.x, partner);
+                zmk.y = __shfl_sync(0xffffffffu, mine.y, partner);
+                if (rt == 0) {
+                    zmk = v[(RP::E - i) % RP::E];
+                }
+                const int k = rt + i * RP::P;
+                if (act && k < m2) {
+                    s.colbuf[r * K::CW + k] = r2c_combine(v[i], zmk, s.half[k]);
                 }
             }
-            group_sync<RP::P>();
+            if (act && rt == 0 && M < m2) {  // the Nyquist output, X[M] = Z[0].x - Z[0].y
+                s.colbuf[r * K::CW + M] = r2c_combine(v[0], v[0], s.half[M]);
+            }
         }
         __syncthreads();
         // Columns: N1-point transforms of the m2 kept columns, only the 2 m1 kept rows written.
@@ -182,13 +197,18 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
             for (int i = 0; i < RP::E; ++i) {
                 const int k = rt + i * RP::P;
-                float2 xk = (act && k < m2) ? s.colbuf[r * K::CW + k] : zero;
-                float2 xmk = (act && M - k < m2) ? s.colbuf[r * K::CW + (M - k)] : zero;
-                if (k == 0) {
-                    xk.y = 0.0f;
-                    xmk.y = 0.0f;
+                const bool has_k = act && k < m2;
+                const bool has_mk = act && M - k < m2;
+                u[i] = zero;
+                if (has_k || has_mk) {  // most of a row's spectrum is zero: skip it whole
+                    float2 xk = has_k ? s.colbuf[r * K::CW + k] : zero;
+                    float2 xmk = has_mk ? s.colbuf[r * K::CW + (M - k)] : zero;
+                    if (k == 0) {
+                        xk.y = 0.0f;
+                        xmk.y = 0.0f;
+                    }
+                    u[i] = c2r_prepare(xk, xmk, s.half[k]);
                 }
-                u[i] = c2r_prepare(xk, xmk, s.half[k]);
             }
             run_passes<RP, true, B>(u, rt, slot, s.twr);
             if (act) {

@@ -34,6 +34,13 @@ __host__ __device__ constexpr int default_threads(int n)
 template <int N>
 using PlanFor = Plan<N, default_e(N), false, default_threads(N)>;
 
+// The inverse complex transform of 1024 points measured fastest with 256-thread CTAs (51 us
+// against 56 us with 128 threads at 2^24 points), unlike the forward one.
+__host__ __device__ constexpr int inverse_threads(int n) { return n == 1024 ? 256 : default_threads(n); }
+
+template <int N>
+using PlanForInv = Plan<N, default_e(N), false, inverse_threads(N)>;
+
 // The plan with the small radix last, for the mirror-paired real-to-complex rows.
 template <int N>
 using PlanR2c = Plan<N, default_e(N), true, default_threads(N)>;
@@ -121,14 +128,15 @@ struct RowEngine {
                 }
                 launch_rows<PL, false, B, Table>(io, batch, s, nullptr);
             } else {
+                using PI = PlanForInv<N>;
                 const C2cIo io{x, y, keep, N, 1.0f / N};
                 if constexpr (stage_c2c(N)) {
                     if (staged && keep == N) {
-                        launch_rows_staged<PL, true, B, Table>(io, batch, s, nullptr);
+                        launch_rows_staged<PI, true, B, Table>(io, batch, s, nullptr);
                         return;
                     }
                 }
-                launch_rows<PL, true, B, Table>(io, batch, s, nullptr);
+                launch_rows<PI, true, B, Table>(io, batch, s, nullptr);
             }
         });
     }

@@ -83,9 +83,10 @@ __host__ __device__ constexpr int plan_tw_entries(int n, int e, bool small_last 
     return plan_tw_offset(n, e, plan_passes(n, e), small_last);
 }
 
-template <int N_, int E_, bool SmallLast_ = false, int MinThreads_ = kMinThreads>
+template <int N_, int E_, bool SmallLast_ = false, int MinThreads_ = kMinThreads, int MinBlocks_ = 1>
 struct Plan {
     static constexpr int N = N_;
+    static constexpr int MIN_BLOCKS = MinBlocks_;  // CTAs per SM the register budget must allow
     static constexpr int E = E_;
     static constexpr bool SmallLast = SmallLast_;
     static_assert(is_pow2(N) && is_pow2(E) && E <= N && E <= 32 && (N == 1 || E >= 2), "bad plan");
@@ -129,6 +130,29 @@ __device__ __forceinline__ void group_sync()
     }
 }
 
+// Entry idx of a pass table computed on chip: W_{L R}^(k r) for idx = r L + k, by sincospif of
+// 2 (k r mod L R) / (L R), a dyadic fraction with at most 15 bits and so exact in float.
+__device__ __forceinline__ float2 computed_pass_twiddle(int idx, int L, int R)
+{
+    const int LR = L * R;
+    const int r = idx / L;
+    const int k = idx - r * L;
+    const float a = 2.0f * static_cast<float>((k * r) & (LR - 1)) / static_cast<float>(LR);
+    float sn = 0.0f;
+    float cs = 1.0f;
+    sincospif(a, &sn, &cs);
+    return make_float2(cs, -sn);
+}
+
+// W_{2n}^k computed on chip (k / n is exact in float for the sizes used).
+__device__ __forceinline__ float2 computed_half_turn(int k, int n)
+{
+    float sn = 0.0f;
+    float cs = 1.0f;
+    sincospif(static_cast<float>(k) / static_cast<float>(n), &sn, &cs);
+    return make_float2(cs, -sn);
+}
+
 // Fills the pass tables: computed on chip (Table == false) or copied from `table`.
 template <class PL, bool Table>
 __device__ __forceinline__ void fill_pass_twiddles(float2* tw, const float2* __restrict__ table)
@@ -141,17 +165,7 @@ __device__ __forceinline__ void fill_pass_twiddles(float2* tw, const float2* __r
             while (s + 1 < PL::PASSES && e >= PL::tw_offset(s + 1)) {
                 ++s;
             }
-            const int idx = e - PL::tw_offset(s);
-            const int L = PL::span(s);
-            const int LR = L * PL::radix(s);
-            const int r = idx / L;
-            const int k = idx - r * L;
-            // 2 (k r mod L R) / (L R) is a dyadic fraction with at most 15 bits: exact in float.
-            const float a = 2.0f * static_cast<float>((k * r) & (LR - 1)) / static_cast<float>(LR);
-            float sn = 0.0f;
-            float cs = 1.0f;
-            sincospif(a, &sn, &cs);
-            tw[e] = make_float2(cs, -sn);
+            tw[e] = computed_pass_twiddle(e - PL::tw_offset(s), PL::span(s), PL::radix(s));
         }
     }
 }
@@ -330,18 +344,24 @@ struct RowCtx {
     const float2* extra; // the Io's shared-memory table
 };
 
-template <class PL, bool Inv, int B, bool Table, class Io>
-__global__ void __launch_bounds__(PL::THREADS)
+template <class PL, bool Inv, int B, bool Table, class Io, bool TwGlobal = false>
+__global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
     row_kernel(const Io io, long long batch, const float2* __restrict__ tw_table,
                const float2* __restrict__ extra_table)
 {
     extern __shared__ float4 smem_raw[];
-    float2* tw = reinterpret_cast<float2*>(smem_raw);
-    float2* extra = tw + PL::TW;
-    float2* bufs = extra + Io::template extra<PL>();
+    // TwGlobal: the tables are read where they lie in global memory (one L1-resident copy per SM
+    // instead of one shared-memory copy per CTA, so more CTAs fit).
+    float2* tw_s = reinterpret_cast<float2*>(smem_raw);
+    float2* extra_s = tw_s + (TwGlobal ? 0 : PL::TW);
+    float2* bufs = extra_s + (TwGlobal ? 0 : Io::template extra<PL>());
+    const float2* tw = TwGlobal ? tw_table : tw_s;
+    const float2* extra = TwGlobal ? extra_table : extra_s;
 
-    fill_pass_twiddles<PL, Table>(tw, tw_table);
-    Io::template prologue<PL, Table>(extra, extra_table);
+    if constexpr (!TwGlobal) {
+        fill_pass_twiddles<PL, Table>(tw_s, tw_table);
+        Io::template prologue<PL, Table>(extra_s, extra_table);
+    }
     __syncthreads();
 
     const int g = threadIdx.x / PL::P;
@@ -391,22 +411,26 @@ __host__ __device__ constexpr int stage_entries()
     return (cmax(PL::G * PL::BUF, Io::template staged_input_entries<PL>()) + 1) & ~1;
 }
 
-template <class PL, bool Inv, int B, bool Table, class Io>
-__global__ void __launch_bounds__(PL::THREADS)
+template <class PL, bool Inv, int B, bool Table, class Io, bool TwGlobal = false>
+__global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
     staged_row_kernel(const Io io, long long batch, const float2* __restrict__ tw_table,
                       const float2* __restrict__ extra_table, unsigned* fault)
 {
     extern __shared__ float4 smem_raw[];
-    constexpr int kExtra = (Io::template extra<PL>() + 1) & ~1;
-    constexpr int kTw = (PL::TW + 1) & ~1;
+    constexpr int kExtra = TwGlobal ? 0 : (Io::template extra<PL>() + 1) & ~1;
+    constexpr int kTw = TwGlobal ? 0 : (PL::TW + 1) & ~1;
     constexpr int kStage = stage_entries<PL, Io>();
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);  // two mbarriers, 16 bytes
-    float2* tw = reinterpret_cast<float2*>(smem_raw + 1);
-    float2* extra = tw + kTw;
-    float2* stages = extra + kExtra;  // 16-byte aligned: every region above is an even count
+    float2* tw_s = reinterpret_cast<float2*>(smem_raw + 1);
+    float2* extra_s = tw_s + kTw;
+    float2* stages = extra_s + kExtra;  // 16-byte aligned: every region above is an even count
+    const float2* tw = TwGlobal ? tw_table : tw_s;
+    const float2* extra = TwGlobal ? extra_table : extra_s;
 
-    fill_pass_twiddles<PL, Table>(tw, tw_table);
-    Io::template prologue<PL, Table>(extra, extra_table);
+    if constexpr (!TwGlobal) {
+        fill_pass_twiddles<PL, Table>(tw_s, tw_table);
+        Io::template prologue<PL, Table>(extra_s, extra_table);
+    }
     if (threadIdx.x == 0) {
         tma::mbar_init(&bars[0], 1);
         tma::mbar_init(&bars[1], 1);
@@ -479,20 +503,21 @@ __global__ void __launch_bounds__(PL::THREADS)
     }
 }
 
-template <class PL, class Io>
+template <class PL, class Io, bool TwGlobal = false>
 constexpr std::size_t staged_smem_bytes()
 {
     return 16
            + sizeof(float2)
-                 * (static_cast<std::size_t>((PL::TW + 1) & ~1) + ((Io::template extra<PL>() + 1) & ~1)
+                 * ((TwGlobal ? 0 : static_cast<std::size_t>((PL::TW + 1) & ~1)
+                                        + ((Io::template extra<PL>() + 1) & ~1))
                     + 2 * static_cast<std::size_t>(stage_entries<PL, Io>()));
 }
 
-template <class PL, class Io>
+template <class PL, class Io, bool TwGlobal = false>
 constexpr std::size_t row_smem_bytes()
 {
     return sizeof(float2)
-           * (static_cast<std::size_t>(PL::TW) + Io::template extra<PL>()
+           * ((TwGlobal ? 0 : static_cast<std::size_t>(PL::TW) + Io::template extra<PL>())
               + static_cast<std::size_t>(PL::G) * PL::BUF);
 }
 
@@ -597,10 +622,7 @@ __device__ __forceinline__ void fill_half_turn(float2* w, const float2* __restri
         if constexpr (Table) {
             w[k] = table[k];
         } else {
-            float sn = 0.0f;
-            float cs = 1.0f;
-            sincospif(static_cast<float>(k) / static_cast<float>(PL::N), &sn, &cs);  // exact ratio
-            w[k] = make_float2(cs, -sn);
+            w[k] = computed_half_turn(k, PL::N);
         }
     }
 }

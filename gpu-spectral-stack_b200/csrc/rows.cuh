@@ -22,10 +22,8 @@ __host__ __device__ constexpr int default_e(int n)
     return n <= 16 ? n : n <= 64 ? 8 : n <= 256 ? 16 : n <= 1024 ? 32 : n <= 8192 ? 16 : 32;
 }
 
-// Threads per CTA (the CTA holds THREADS / P transforms). Measured on B200 at 2^24 points per
-// call: for 1024 and 2048 points, 128-thread CTAs (4 and 1 transforms) leave more CTAs per SM
-// than 256-thread ones, whose twiddle tables and buffers fill shared memory; that beats larger
-// CTAs by 7-10 %.
+// Threads per CTA for the column and fused 2D kernels' plans (PlanFor); row kernels use
+// row_choice below.
 __host__ __device__ constexpr int default_threads(int n)
 {
     return (n == 1024 || n == 2048) ? 128 : kMinThreads;
@@ -34,55 +32,105 @@ __host__ __device__ constexpr int default_threads(int n)
 template <int N>
 using PlanFor = Plan<N, default_e(N), false, default_threads(N)>;
 
-// The inverse complex transform of 1024 points measured fastest with 256-thread CTAs (51 us
-// against 56 us with 128 threads at 2^24 points), unlike the forward one.
-__host__ __device__ constexpr int inverse_threads(int n) { return n == 1024 ? 256 : default_threads(n); }
+// --- row kernel choices ------------------------------------------------------------------------
+//
+// Per transform kind and size (n complex points per transform; M = n / 2 for the real kinds):
+// threads per CTA, the CTAs per SM the register budget must allow, whether the twiddle tables
+// are copied into shared memory per CTA or read from global memory (one L1-resident copy per SM),
+// and whether the input is prefetched with bulk copies (the staged kernel). Each entry is the
+// best of a sweep on B200 at 2^24 points per call. The pattern: reading the twiddles from global
+// memory halves the shared memory of the real-transform kernels and lets the compiler hoist the
+// twiddle loads past the exchanges' barriers (1024 real points: 38.9 -> 30.0 us; 4096: 39.1 ->
+// 31.2 us; its inverse 41.6 -> 29.0 us), while the complex transforms up to 1024 points, whose
+// tables are small, gain little or nothing from it. The bulk-copy prefetch pays only for complex
+// transforms of 2048 and 4096 points, which span eight warps.
 
-template <int N>
-using PlanForInv = Plan<N, default_e(N), false, inverse_threads(N)>;
+enum class RowKind { C2c, R2c, C2r };
 
-// The plan with the small radix last, for the mirror-paired real-to-complex rows.
-template <int N>
-using PlanR2c = Plan<N, default_e(N), true, default_threads(N)>;
+struct RowChoice {
+    int threads;
+    int min_blocks;
+    bool smem_twiddles;
+    bool staged;
+};
 
-// Complex rows: the bulk-copy prefetch pays where a transform spans several warps; for 1024
-// points (one warp per transform, 4 CTAs of 4 transforms per SM) direct loads measured 10 %
-// faster than the staged kernel, whose second buffer halves the CTAs that fit.
-__host__ __device__ constexpr bool stage_c2c(int n) { return n >= 2048; }
+__host__ __device__ constexpr RowChoice row_choice(RowKind k, int n)
+{
+    if (k == RowKind::C2c) {
+        return n <= 64   ? RowChoice{kMinThreads, 1, true, false}
+             : n <= 512  ? RowChoice{128, 4, false, false}
+             : n == 1024 ? RowChoice{128, 4, true, false}
+             : n == 2048 ? RowChoice{kMinThreads, 1, false, true}
+                         : RowChoice{kMinThreads, 2, true, true};
+    }
+    return n <= 32     ? RowChoice{kMinThreads, 1, true, false}
+         : n == 64     ? RowChoice{kMinThreads, 1, false, false}
+         : n == 512    ? RowChoice{128, k == RowKind::R2c ? 3 : 4, k == RowKind::R2c, false}
+         : n <= 1024   ? RowChoice{128, 4, false, false}
+         : n == 2048   ? RowChoice{128, k == RowKind::R2c ? 5 : 6, false, false}
+                       : RowChoice{kMinThreads, 2, false, false};
+}
 
-template <class PL, bool Inv, int B, bool Table, class Io>
+template <RowKind K, int N, bool SmallLast = false>
+using RowPlan = Plan<N, default_e(N), SmallLast, row_choice(K, N).threads, row_choice(K, N).min_blocks>;
+
+// The twiddle tables a row kernel reads: the correctly rounded host tables (Table), else the
+// on-chip computed ones, in global memory when the kernel does not fill its own shared copy.
+template <class PL, bool Table, bool SmemTw>
+const float2* row_pass_table()
+{
+    if constexpr (Table) {
+        return twiddles::pass_table(PL::N, PL::E, PL::SmallLast);
+    } else if constexpr (SmemTw) {
+        return nullptr;
+    } else {
+        return twiddles::pass_table_computed(PL::N, PL::E, PL::SmallLast);
+    }
+}
+
+template <int M, bool Table, bool SmemTw>
+const float2* row_half_turn()
+{
+    if constexpr (Table) {
+        return twiddles::half_turn(M);
+    } else if constexpr (SmemTw) {
+        return nullptr;
+    } else {
+        return twiddles::half_turn_computed(M);
+    }
+}
+
+template <class PL, bool Inv, int B, bool Table, bool SmemTw, class Io>
 void launch_rows(const Io& io, long long batch, cudaStream_t stream, const float2* extra_table)
 {
     if (batch <= 0) {
         return;
     }
-    auto kernel = row_kernel<PL, Inv, B, Table, Io>;
-    constexpr std::size_t smem = row_smem_bytes<PL, Io>();
+    auto kernel = row_kernel<PL, Inv, B, Table, Io, !SmemTw>;
+    constexpr std::size_t smem = row_smem_bytes<PL, Io, !SmemTw>();
     static std::atomic<int> cache[kMaxDevices];
-    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E, PL::SmallLast) : nullptr;
+    const float2* tw = row_pass_table<PL, Table, SmemTw>();
     const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem,
                                           cache, (batch + PL::G - 1) / PL::G);
     kernel<<<grid, PL::THREADS, smem, stream>>>(io, batch, tw, extra_table);
     SPECTRAL_CUDA(cudaGetLastError());
 }
 
-// The staged kernel (bulk-copy prefetch, engine.cuh) for sizes where it pays, when the input
-// satisfies cp.async.bulk's rules: a 16-byte aligned source and whole 16-byte tiles.
-constexpr int kMinStagedN = 64;
-
+// The staged kernel (bulk-copy prefetch, engine.cuh), when the input satisfies cp.async.bulk's
+// rules: a 16-byte aligned source and whole 16-byte tiles.
 inline bool aligned16(const void* p) { return (reinterpret_cast<unsigned long long>(p) & 15u) == 0; }
 
-template <class PL, bool Inv, int B, bool Table, class Io>
+template <class PL, bool Inv, int B, bool Table, bool SmemTw, class Io>
 void launch_rows_staged(const Io& io, long long batch, cudaStream_t stream, const float2* extra_table)
 {
     if (batch <= 0) {
         return;
     }
-    auto kernel = staged_row_kernel<PL, Inv, B, Table, Io>;
-    constexpr std::size_t smem = staged_smem_bytes<PL, Io>();
+    auto kernel = staged_row_kernel<PL, Inv, B, Table, Io, !SmemTw>;
+    constexpr std::size_t smem = staged_smem_bytes<PL, Io, !SmemTw>();
     static_assert(smem <= 227 * 1024, "staged tile does not fit in shared memory");
     static std::atomic<int> cache[kMaxDevices];
-    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E, PL::SmallLast) : nullptr;
+    const float2* tw = row_pass_table<PL, Table, SmemTw>();
     const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem,
                                           cache, (batch + PL::G - 1) / PL::G);
     kernel<<<grid, PL::THREADS, smem, stream>>>(io, batch, tw, extra_table, device_fault_word());
@@ -116,27 +164,26 @@ struct RowEngine {
     {
         dispatch_pow2<2, kMaxRowN>(n, [&](auto n_) {
             constexpr int N = decltype(n_)::value;
-            using PL = PlanFor<N>;
-            const bool staged = stage_c2c(N) && aligned16(x);
-            if (d == Direction::Forward) {
-                const C2cIo io{x, y, N, keep, 1.0f};
-                if constexpr (stage_c2c(N)) {
-                    if (staged) {
-                        launch_rows_staged<PL, false, B, Table>(io, batch, s, nullptr);
-                        return;
+            constexpr RowChoice rc = row_choice(RowKind::C2c, N);
+            using PL = RowPlan<RowKind::C2c, N>;
+            const bool inv = d == Direction::Inverse;
+            const C2cIo io = inv ? C2cIo{x, y, keep, N, 1.0f / N} : C2cIo{x, y, N, keep, 1.0f};
+            // Staged tiles are whole unpruned input rows.
+            const bool staged = rc.staged && aligned16(x) && (!inv || keep == N);
+            if constexpr (rc.staged && N >= 64) {
+                if (staged) {
+                    if (inv) {
+                        launch_rows_staged<PL, true, B, Table, rc.smem_twiddles>(io, batch, s, nullptr);
+                    } else {
+                        launch_rows_staged<PL, false, B, Table, rc.smem_twiddles>(io, batch, s, nullptr);
                     }
+                    return;
                 }
-                launch_rows<PL, false, B, Table>(io, batch, s, nullptr);
+            }
+            if (inv) {
+                launch_rows<PL, true, B, Table, rc.smem_twiddles>(io, batch, s, nullptr);
             } else {
-                using PI = PlanForInv<N>;
-                const C2cIo io{x, y, keep, N, 1.0f / N};
-                if constexpr (stage_c2c(N)) {
-                    if (staged && keep == N) {
-                        launch_rows_staged<PI, true, B, Table>(io, batch, s, nullptr);
-                        return;
-                    }
-                }
-                launch_rows<PI, true, B, Table>(io, batch, s, nullptr);
+                launch_rows<PL, false, B, Table, rc.smem_twiddles>(io, batch, s, nullptr);
             }
         });
     }
@@ -149,28 +196,15 @@ struct RowEngine {
     {
         dispatch_pow2<1, kMaxRowN>(n / 2, [&](auto m_) {
             constexpr int M = decltype(m_)::value;
-            const float2* w = Table ? twiddles::half_turn(M) : nullptr;
+            constexpr RowChoice rc = row_choice(RowKind::R2c, M);
+            const float2* w = row_half_turn<M, Table, rc.smem_twiddles>();
             const auto* xz = reinterpret_cast<const float2*>(x);
-            using PP = PlanR2c<M>;
+            using PP = RowPlan<RowKind::R2c, M, true>;
             if constexpr (M >= 32 && PP::kPairLast) {
-                const R2cPairIo io{xz, y, keep};
-                if constexpr (M >= kMinStagedN) {
-                    if (aligned16(x)) {
-                        launch_rows_staged<PP, false, B, Table>(io, batch, s, w);
-                        return;
-                    }
-                }
-                launch_rows<PP, false, B, Table>(io, batch, s, w);
+                launch_rows<PP, false, B, Table, rc.smem_twiddles>(R2cPairIo{xz, y, keep}, batch, s, w);
             } else {
-                using PL = PlanFor<M>;
-                const R2cIo io{xz, y, keep};
-                if constexpr (M >= kMinStagedN) {
-                    if (aligned16(x)) {
-                        launch_rows_staged<PL, false, B, Table>(io, batch, s, w);
-                        return;
-                    }
-                }
-                launch_rows<PL, false, B, Table>(io, batch, s, w);
+                using PL = RowPlan<RowKind::R2c, M>;
+                launch_rows<PL, false, B, Table, rc.smem_twiddles>(R2cIo{xz, y, keep}, batch, s, w);
             }
         });
     }
@@ -183,30 +217,14 @@ struct RowEngine {
     {
         dispatch_pow2<1, kMaxRowN>(n / 2, [&](auto m_) {
             constexpr int M = decltype(m_)::value;
-            using PL = PlanFor<M>;
-            const float2* w = Table ? twiddles::half_turn(M) : nullptr;
+            constexpr RowChoice rc = row_choice(RowKind::C2r, M);
+            using PL = RowPlan<RowKind::C2r, M>;
+            const float2* w = row_half_turn<M, Table, rc.smem_twiddles>();
             auto* yz = reinterpret_cast<float2*>(y);
-            // The staged copy of a tile is rounded to 16 bytes; with batch * keep even and x
-            // aligned the rounding never reaches past the end of x.
-            const bool staged = M >= kMinStagedN && aligned16(x) && (batch * keep) % 2 == 0;
             if constexpr (M >= 32 && PL::kPairFirst) {
-                const C2rPairIo io{x, yz, keep, 1.0f / M};
-                if constexpr (M >= kMinStagedN) {
-                    if (staged) {
-                        launch_rows_staged<PL, true, B, Table>(io, batch, s, w);
-                        return;
-                    }
-                }
-                launch_rows<PL, true, B, Table>(io, batch, s, w);
+                launch_rows<PL, true, B, Table, rc.smem_twiddles>(C2rPairIo{x, yz, keep, 1.0f / M}, batch, s, w);
             } else {
-                const C2rIo io{x, yz, keep, 1.0f / M};
-                if constexpr (M >= kMinStagedN) {
-                    if (staged) {
-                        launch_rows_staged<PL, true, B, Table>(io, batch, s, w);
-                        return;
-                    }
-                }
-                launch_rows<PL, true, B, Table>(io, batch, s, w);
+                launch_rows<PL, true, B, Table, rc.smem_twiddles>(C2rIo{x, yz, keep, 1.0f / M}, batch, s, w);
             }
         });
     }

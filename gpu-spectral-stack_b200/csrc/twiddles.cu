@@ -34,8 +34,11 @@ float2 forward_factor(long long j, long long m)
     return make_float2(static_cast<float>(w.c), static_cast<float>(-w.s));
 }
 
-template <class Build>
-const float2* get(const Key& key, long long count, Build&& build)
+// Reserves `count` entries of the pool for `key` (16-byte aligned) and fills them with
+// fill(device pointer, offset in the pool); returns the cached table when `key` was built before
+// on this device.
+template <class Fill>
+const float2* get_filled(const Key& key, long long count, Fill&& fill)
 {
     int device = 0;
     SPECTRAL_CUDA(cudaGetDevice(&device));
@@ -50,19 +53,59 @@ const float2* get(const Key& key, long long count, Build&& build)
         SPECTRAL_CUDA(cudaGetSymbolAddress(&p, g_pool));
         dt.base = static_cast<float2*>(p);
     }
-    const long long aligned = (dt.used + 1) & ~1LL;  // 16-byte aligned tables
+    const long long aligned = (dt.used + 1) & ~1LL;
     if (aligned + count > kPoolEntries) {
         throw InvalidArgument("twiddle tables: pool exhausted");
     }
-    std::vector<float2> host(static_cast<std::size_t>(count));
-    build(host);
-    SPECTRAL_CUDA(cudaMemcpyToSymbol(g_pool, host.data(), host.size() * sizeof(float2),
-                                     static_cast<std::size_t>(aligned) * sizeof(float2),
-                                     cudaMemcpyHostToDevice));
-    const float2* ptr = dt.base + aligned;
+    float2* ptr = dt.base + aligned;
+    fill(ptr, aligned);
     dt.used = aligned + count;
     dt.tables.emplace(key, ptr);
     return ptr;
+}
+
+template <class Build>
+const float2* get(const Key& key, long long count, Build&& build)
+{
+    return get_filled(key, count, [&](float2*, long long offset) {
+        std::vector<float2> host(static_cast<std::size_t>(count));
+        build(host);
+        SPECTRAL_CUDA(cudaMemcpyToSymbol(g_pool, host.data(), host.size() * sizeof(float2),
+                                         static_cast<std::size_t>(offset) * sizeof(float2),
+                                         cudaMemcpyHostToDevice));
+    });
+}
+
+__global__ void computed_pass_kernel(float2* out, int n, int e, bool small_last)
+{
+    const int passes = engine::plan_passes(n, e);
+    const int entries = engine::plan_tw_entries(n, e, small_last);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < entries; i += gridDim.x * blockDim.x) {
+        int s = 1;
+        while (s + 1 < passes && i >= engine::plan_tw_offset(n, e, s + 1, small_last)) {
+            ++s;
+        }
+        out[i] = engine::computed_pass_twiddle(i - engine::plan_tw_offset(n, e, s, small_last),
+                                               engine::plan_span(n, e, s, small_last),
+                                               engine::plan_radix(n, e, s, small_last));
+    }
+}
+
+__global__ void computed_half_turn_kernel(float2* out, int n)
+{
+    for (int k = blockIdx.x * blockDim.x + threadIdx.x; k <= n; k += gridDim.x * blockDim.x) {
+        out[k] = engine::computed_half_turn(k, n);
+    }
+}
+
+// Runs a table-filling kernel on the legacy default stream and waits for it, so the table is
+// complete before any stream uses it.
+template <class Launch>
+void fill_on_device(Launch&& launch)
+{
+    launch();
+    SPECTRAL_CUDA(cudaGetLastError());
+    SPECTRAL_CUDA(cudaStreamSynchronize(0));
 }
 
 }  // namespace
@@ -83,6 +126,23 @@ const float2* pass_table(int n, int e, bool small_last)
                 }
             }
         }
+    });
+}
+
+const float2* pass_table_computed(int n, int e, bool small_last)
+{
+    const int entries = engine::plan_tw_entries(n, e, small_last);
+    return get_filled(Key{small_last ? 5 : 4, n, e}, entries < 1 ? 1 : entries, [&](float2* p, long long) {
+        if (entries > 0) {
+            fill_on_device([&] { computed_pass_kernel<<<(entries + 255) / 256, 256>>>(p, n, e, small_last); });
+        }
+    });
+}
+
+const float2* half_turn_computed(int n)
+{
+    return get_filled(Key{6, n, 0}, n + 1, [&](float2* p, long long) {
+        fill_on_device([&] { computed_half_turn_kernel<<<(n + 256) / 256, 256>>>(p, n); });
     });
 }
 

@@ -20,6 +20,13 @@ const float2* pass_table(int n, int e, bool small_last = false);
 // W_{2n}^k = exp(-pi i k / n) for k = 0 .. n: n + 1 entries (real-transform combine).
 const float2* half_turn(int n);
 
+// The same two tables computed on the GPU with sincospif, the formula the kernels use when they
+// fill their shared-memory tables themselves (engine.cuh: computed_pass_twiddle,
+// computed_half_turn). Kernels that read their tables from global memory use these for the
+// computed-twiddle variants. Built by a kernel on first use per device, then synchronised.
+const float2* pass_table_computed(int n, int e, bool small_last = false);
+const float2* half_turn_computed(int n);
+
 // W_total^j = exp(-2 pi i j / total) for j = 0 .. count-1 (the four-step inter-pass factors are
 // products of two such tables).
 const float2* turn(long long total, int count);

@@ -1,0 +1,58 @@
+"""The slab-decomposed 2D transform across real ranks: one process per GPU, NCCL all-to-all over
+NVLink, every rank checking its column slab (forward) and its row slab (inverse) against the
+float64 oracle. Needs two GPUs; skipped otherwise (the one-GPU emulation is tests/test_slab.py and
+the index arithmetic on CPU ranks is tests/test_distributed.py)."""
+
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, n: int) -> None:
+    import torch.distributed as dist
+
+    from oracle.policy import assert_transform_close, fft_tolerance
+    from spectral.distributed import fft2_slab
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        rng = np.random.default_rng(5)
+        x = (rng.standard_normal((n, n)) + 1j * rng.standard_normal((n, n))).astype(np.complex64)
+        rows = n // world
+        w = n // world
+        local = torch.from_numpy(x[rank * rows:(rank + 1) * rows]).cuda()
+        cols = fft2_slab(local)
+        expected = np.fft.fft2(x.astype(np.complex128))[:, rank * w:(rank + 1) * w]
+        got = cols.cpu().numpy()
+        # The rank's share of one n x n transform: its norm-wise error stays within the bound of
+        # the whole transform.
+        assert_transform_close(got[None], expected[None], n * n, axes=(-2, -1))
+        back = fft2_slab(cols, inverse=True)
+        assert_transform_close(back.cpu().numpy()[None], x[rank * rows:(rank + 1) * rows][None],
+                               n * n, axes=(-2, -1), tol=2 * fft_tolerance(n * n))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n", [1024, 4096])
+def test_slab_across_two_gpus(n):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    torch.multiprocessing.spawn(_rank_main, args=(2, _free_port(), n), nprocs=2, join=True)

@@ -28,6 +28,7 @@
 #include "columns.cuh"
 
 #include <climits>
+#include <type_traits>
 
 namespace spectral {
 namespace {
@@ -45,6 +46,7 @@ using SlabPlan = Plan<N, (N <= 4096 ? default_e(N) : N == 8192 ? 16 : 32), false
 // chunked; inverse reads chunked and writes natural.
 template <bool Inv>
 struct SlabRowIo {
+    static constexpr bool kPeer = false;
     const float2* x;
     float2* y;
     long long rows;  // rows per rank
@@ -82,9 +84,63 @@ struct SlabRowIo {
     }
 };
 
-template <class PL, bool Inv>
+// Rows of a slab exchanged through peer memory instead of an all-to-all: the chunked side lives
+// on the ranks themselves. peer[s] is rank s's n x w column-slab buffer mapped into this GPU's
+// address space (CUDA IPC over NVLink); this rank's rows are rows rank * rows .. of every one.
+// Forward: the row transforms store chunk s of each row straight into peer[s] (plain stores over
+// NVLink, coalesced in runs of at least 32 values). Inverse: the row transforms load chunk s of
+// each row from peer[s]. The caller orders the ranks around the launch (a collective between the
+// row and column kernels).
+constexpr int kMaxPeerRanks = 8;
+
+struct PeerSlabs {
+    float2* p[kMaxPeerRanks];
+};
+
+template <bool Inv>
+struct SlabPeerRowIo {
+    static constexpr bool kPeer = true;
+    const float2* x;  // forward: the rank's rows
+    float2* y;        // inverse: the rank's rows
+    PeerSlabs peer;
+    long long rows;   // rows per rank
+    int rank;
+    int wlog;         // log2 of the columns per chunk
+    float scale;
+
+    __device__ __forceinline__ long long at(long long row, int k) const
+    {
+        return ((static_cast<long long>(rank) * rows + row) << wlog) + (k & ((1 << wlog) - 1));
+    }
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], long long row, int t) const
+    {
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const int k = t + i * PL::P;
+            v[i] = Inv ? peer.p[k >> wlog][at(row, k)] : x[row * PL::N + k];
+        }
+    }
+
+    template <class PL>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], long long row, int t) const
+    {
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const int k = t + i * PL::P;
+            if constexpr (Inv) {
+                y[row * PL::N + k] = cscale(v[i], scale);
+            } else {
+                peer.p[k >> wlog][at(row, k)] = v[i];
+            }
+        }
+    }
+};
+
+template <class PL, bool Inv, class Io>
 __global__ void __launch_bounds__(PL::THREADS)
-    slab_row_kernel(const SlabRowIo<Inv> io, const float2* __restrict__ tw)
+    slab_row_kernel(const Io io, const float2* __restrict__ tw)
 {
     extern __shared__ float4 smem_raw[];
     float2* bufs = reinterpret_cast<float2*>(smem_raw);
@@ -109,16 +165,19 @@ __global__ void __launch_bounds__(PL::THREADS)
             io.template store<PL>(v, row, t);
         }
     }
+    if constexpr (Io::kPeer && !Inv) {
+        __threadfence_system();  // stores into peers' memory are complete before the kernel ends
+    }
 }
 
-template <bool Inv>
-void slab_rows(const float2* x, float2* y, int n, long long rows, int ranks, cudaStream_t s)
+template <bool Inv, class MakeIo>
+void slab_rows(int n, long long rows, cudaStream_t s, MakeIo&& make_io)
 {
     dispatch_pow2<2, kMaxSlabN>(n, [&](auto n_) {
         constexpr int N = decltype(n_)::value;
         using PL = SlabPlan<N>;
-        const SlabRowIo<Inv> io{x, y, rows, ilog2(n / ranks), Inv ? 1.0f / N : 1.0f};
-        auto kernel = slab_row_kernel<PL, Inv>;
+        const auto io = make_io(static_cast<float>(Inv ? 1.0 / N : 1.0));
+        auto kernel = slab_row_kernel<PL, Inv, std::decay_t<decltype(io)>>;
         constexpr std::size_t smem = sizeof(float2) * static_cast<std::size_t>(PL::G) * PL::BUF;
         static std::atomic<int> cache[kMaxDevices];
         const float2* tw = twiddles::pass_table(PL::N, PL::E);
@@ -289,10 +348,55 @@ extern "C" int spectral_slab_rows(const void* x, void* y, int n, long long rows,
         const auto* xs = static_cast<const float2*>(x);
         auto* ys = static_cast<float2*>(y);
         const auto s = static_cast<cudaStream_t>(stream);
+        const int wlog = ilog2(n / ranks);
         if (inverse) {
-            slab_rows<true>(xs, ys, n, rows, ranks, s);
+            slab_rows<true>(n, rows, s, [&](float sc) { return SlabRowIo<true>{xs, ys, rows, wlog, sc}; });
         } else {
-            slab_rows<false>(xs, ys, n, rows, ranks, s);
+            slab_rows<false>(n, rows, s, [&](float sc) { return SlabRowIo<false>{xs, ys, rows, wlog, sc}; });
+        }
+    });
+}
+
+extern "C" int spectral_slab_rows_peer(const void* x, void* y, void* const* peers, int n,
+                                       long long rows, int rank, int ranks, int inverse,
+                                       void* stream)
+{
+    using namespace spectral;
+    return slab_guarded([&] {
+        check_slab(n, ranks);
+        if (ranks > kMaxPeerRanks) {
+            throw InvalidArgument("fft2_slab: the peer exchange takes at most "
+                                  + std::to_string(kMaxPeerRanks) + " ranks, got " + std::to_string(ranks));
+        }
+        if (rank < 0 || rank >= ranks) {
+            throw InvalidArgument("fft2_slab: rank " + std::to_string(rank) + " outside 0 .. "
+                                  + std::to_string(ranks - 1));
+        }
+        if (rows < 1 || rows * ranks != n) {
+            throw InvalidArgument("fft2_slab: rows * ranks must equal n");
+        }
+        if (peers == nullptr) {
+            throw InvalidArgument("fft2_slab: peers must list one buffer per rank");
+        }
+        PeerSlabs ps = {};
+        for (int q = 0; q < ranks; ++q) {
+            if (peers[q] == nullptr) {
+                throw InvalidArgument("fft2_slab: peer buffer " + std::to_string(q) + " is null");
+            }
+            ps.p[q] = static_cast<float2*>(peers[q]);
+        }
+        const auto s = static_cast<cudaStream_t>(stream);
+        const int wlog = ilog2(n / ranks);
+        if (inverse) {
+            auto* ys = static_cast<float2*>(y);
+            slab_rows<true>(n, rows, s, [&](float sc) {
+                return SlabPeerRowIo<true>{nullptr, ys, ps, rows, rank, wlog, sc};
+            });
+        } else {
+            const auto* xs = static_cast<const float2*>(x);
+            slab_rows<false>(n, rows, s, [&](float sc) {
+                return SlabPeerRowIo<false>{xs, nullptr, ps, rows, rank, wlog, sc};
+            });
         }
     });
 }

@@ -60,6 +60,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_irfft2_modes": (_i, [_s, _p, _p, _i, _i, _i, _i, _ll, _p, _p]),
     "spectral_slab_rows": (_i, [_p, _p, _i, _ll, _i, _i, _p]),
     "spectral_slab_columns": (_i, [_p, _p, _i, _i, _i, _p]),
+    "spectral_slab_rows_peer": (_i, [_p, _p, ctypes.POINTER(_p), _i, _ll, _i, _i, _i, _p]),
+    "spectral_ipc_alloc": (_i, [ctypes.c_ulonglong, ctypes.POINTER(_p), _p]),
+    "spectral_ipc_open": (_i, [_p, ctypes.POINTER(_p)]),
+    "spectral_ipc_close": (_i, [_p]),
+    "spectral_ipc_free": (_i, [_p]),
     "spectral_mode_contract": (_i, [_p, _p, _p, _ll, _i, _i, _ll, _p]),
 }
 

@@ -171,6 +171,29 @@ SPECTRAL_API int spectral_slab_rows(const void* x, void* y, int n, long long row
 SPECTRAL_API int spectral_slab_columns(void* x, void* y, int n, int width, int inverse,
                                        void* stream);
 
+/* The row stage with the exchange done in the same kernel through peer memory instead of an
+ * all-to-all (no counterpart in the reference, which has no multi-GPU code). peers[s] (s = 0 ..
+ * ranks-1, at most 8) is rank s's n x w column-slab buffer, mapped into this GPU's address space
+ * (spectral_ipc_open; peers[rank] is this rank's own buffer). Forward: the row transforms of x
+ * (this rank's rows x n) store chunk s of every row straight into peers[s], rows rank * rows ..;
+ * y is unused. Inverse: the row transforms load chunk s of every row from peers[s] (the column
+ * slabs after spectral_slab_columns(inverse)) and write this rank's rows to y; x is unused. The
+ * ranks must be ordered around the call: every rank's writes (forward) or column stage (inverse)
+ * complete before any rank reads them, e.g. by a collective on the same stream. */
+SPECTRAL_API int spectral_slab_rows_peer(const void* x, void* y, void* const* peers, int n,
+                                         long long rows, int rank, int ranks, int inverse,
+                                         void* stream);
+
+/* Device buffers shared between the processes of one node through CUDA IPC, for the buffers
+ * spectral_slab_rows_peer addresses: allocate (cudaMalloc on the current device) and export a
+ * SPECTRAL_IPC_HANDLE_BYTES-byte handle; map another process's handle (peer access enabled on
+ * demand); unmap; free. */
+#define SPECTRAL_IPC_HANDLE_BYTES 64
+SPECTRAL_API int spectral_ipc_alloc(unsigned long long bytes, void** ptr, void* handle);
+SPECTRAL_API int spectral_ipc_open(const void* handle, void** ptr);
+SPECTRAL_API int spectral_ipc_close(void* ptr);
+SPECTRAL_API int spectral_ipc_free(void* ptr);
+
 /* --- per-mode channel contraction of an FNO spectral convolution --------------------------- */
 
 /* out[b, o, m] = sum_i x[b, i, m] * w[i, o, m] over complex values: x (batch, cin, modes),

@@ -1,6 +1,6 @@
-"""The slab-decomposed 2D transform across real ranks: one process per GPU, NCCL all-to-all over
-NVLink, every rank checking its column slab (forward) and its row slab (inverse) against the
-float64 oracle. Needs two GPUs; skipped otherwise (the one-GPU emulation is tests/test_slab.py and
+"""The slab-decomposed 2D transform across real ranks: one process per GPU, the exchange by NCCL
+all-to-all and by peer memory over NVLink, every rank checking its column slab (forward) and its
+row slab (inverse) against the float64 oracle. Needs two GPUs; skipped otherwise (the one-GPU emulation is tests/test_slab.py and
 the index arithmetic on CPU ranks is tests/test_distributed.py)."""
 
 import os
@@ -24,7 +24,7 @@ def _rank_main(rank: int, world: int, port: int, n: int) -> None:
     import torch.distributed as dist
 
     from oracle.policy import assert_transform_close, fft_tolerance
-    from spectral.distributed import fft2_slab
+    from spectral.distributed import PeerSlab, fft2_slab
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -46,6 +46,15 @@ def _rank_main(rank: int, world: int, port: int, n: int) -> None:
         back = fft2_slab(cols, inverse=True)
         assert_transform_close(back.cpu().numpy()[None], x[rank * rows:(rank + 1) * rows][None],
                                n * n, axes=(-2, -1), tol=2 * fft_tolerance(n * n))
+        # The same through peer memory, twice in a row (both receive buffers), and bit for bit
+        # what the all-to-all path gives: the kernels and their order are the same.
+        plan = PeerSlab(n)
+        for _ in range(2):
+            pcols = plan.forward(local)
+            assert torch.equal(pcols, cols)
+            pback = plan.inverse(pcols)
+            assert torch.equal(pback, back)
+        plan.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -37,7 +37,10 @@ using PlanFor = Plan<N, default_e(N), false, default_threads(N)>;
 // Per transform kind and size (n complex points per transform; M = n / 2 for the real kinds):
 // threads per CTA, the CTAs per SM the register budget must allow, whether the twiddle tables
 // are copied into shared memory per CTA or read from global memory (one L1-resident copy per SM),
-// and whether the input is prefetched with bulk copies (the staged kernel). Each entry is the
+// whether the input is prefetched with bulk copies (the staged kernel), and whether the grid is
+// persistent (every resident slot once, walking the batch) or one CTA per tile of transforms
+// (no per-CTA set-up left once the tables are in global memory, and the hardware scheduler
+// balances the last wave: 1024-point complex transforms 47.3 -> 44.5 us). Each entry is the
 // best of a sweep on B200 at 2^24 points per call. The pattern: reading the twiddles from global
 // memory halves the shared memory of the real-transform kernels and lets the compiler hoist the
 // twiddle loads past the exchanges' barriers (1024 real points: 38.9 -> 30.0 us; 4096: 39.1 ->
@@ -52,23 +55,41 @@ struct RowChoice {
     int min_blocks;
     bool smem_twiddles;
     bool staged;
+    bool persistent;
 };
 
 __host__ __device__ constexpr RowChoice row_choice(RowKind k, int n)
 {
     if (k == RowKind::C2c) {
-        return n <= 64   ? RowChoice{kMinThreads, 1, true, false}
-             : n <= 512  ? RowChoice{128, 4, false, false}
-             : n == 1024 ? RowChoice{128, 4, true, false}
-             : n == 2048 ? RowChoice{kMinThreads, 1, false, true}
-                         : RowChoice{kMinThreads, 2, true, true};
+        return n <= 8    ? RowChoice{kMinThreads, 1, true, false, false}
+             : n <= 64   ? RowChoice{kMinThreads, 1, true, false, true}
+             : n == 128  ? RowChoice{128, 4, false, false, true}
+             : n <= 1024 ? RowChoice{128, 4, false, false, false}
+             : n == 2048 ? RowChoice{kMinThreads, 1, false, true, true}
+                         : RowChoice{kMinThreads, 2, true, true, true};
     }
-    return n <= 32     ? RowChoice{kMinThreads, 1, true, false}
-         : n == 64     ? RowChoice{kMinThreads, 1, false, false}
-         : n == 512    ? RowChoice{128, k == RowKind::R2c ? 3 : 4, k == RowKind::R2c, false}
-         : n <= 1024   ? RowChoice{128, 4, false, false}
-         : n == 2048   ? RowChoice{128, k == RowKind::R2c ? 5 : 6, false, false}
-                       : RowChoice{kMinThreads, 2, false, false};
+    const bool r2c = k == RowKind::R2c;
+    return n <= 8      ? RowChoice{kMinThreads, 1, !r2c, false, !r2c}
+         : n == 16     ? RowChoice{kMinThreads, 1, !r2c, false, false}
+         : n == 32     ? RowChoice{kMinThreads, 1, true, false, true}
+         : n == 64     ? RowChoice{kMinThreads, 1, false, false, true}
+         : n == 512    ? RowChoice{128, r2c ? 3 : 4, r2c, false, true}
+         : n <= 1024   ? RowChoice{128, 4, false, false, true}
+         : n == 2048   ? RowChoice{128, r2c ? 4 : 6, false, false, r2c}
+                       : RowChoice{kMinThreads, 2, false, false, true};
+}
+
+// Grid of a row launch: persistent (resident slots) or one CTA per tile. Either way the kernel
+// walks the batch with a grid stride, and the shared-memory opt-in is made once.
+inline unsigned row_grid(const void* kernel, int threads, std::size_t smem, std::atomic<int>* cache,
+                         long long tiles, bool persistent)
+{
+    if (persistent) {
+        return persistent_grid(kernel, threads, smem, cache, tiles);
+    }
+    resident_ctas(kernel, threads, smem, cache, current_device());
+    constexpr long long kMaxGrid = 1LL << 30;
+    return static_cast<unsigned>(tiles < 1 ? 1 : tiles < kMaxGrid ? tiles : kMaxGrid);
 }
 
 template <RowKind K, int N, bool SmallLast = false>
@@ -100,7 +121,7 @@ const float2* row_half_turn()
     }
 }
 
-template <class PL, bool Inv, int B, bool Table, bool SmemTw, class Io>
+template <class PL, bool Inv, int B, bool Table, bool SmemTw, bool Persistent = true, class Io>
 void launch_rows(const Io& io, long long batch, cudaStream_t stream, const float2* extra_table)
 {
     if (batch <= 0) {
@@ -110,8 +131,8 @@ void launch_rows(const Io& io, long long batch, cudaStream_t stream, const float
     constexpr std::size_t smem = row_smem_bytes<PL, Io, !SmemTw>();
     static std::atomic<int> cache[kMaxDevices];
     const float2* tw = row_pass_table<PL, Table, SmemTw>();
-    const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem,
-                                          cache, (batch + PL::G - 1) / PL::G);
+    const unsigned grid = row_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem, cache,
+                                   (batch + PL::G - 1) / PL::G, Persistent);
     kernel<<<grid, PL::THREADS, smem, stream>>>(io, batch, tw, extra_table);
     SPECTRAL_CUDA(cudaGetLastError());
 }
@@ -181,9 +202,9 @@ struct RowEngine {
                 }
             }
             if (inv) {
-                launch_rows<PL, true, B, Table, rc.smem_twiddles>(io, batch, s, nullptr);
+                launch_rows<PL, true, B, Table, rc.smem_twiddles, rc.persistent>(io, batch, s, nullptr);
             } else {
-                launch_rows<PL, false, B, Table, rc.smem_twiddles>(io, batch, s, nullptr);
+                launch_rows<PL, false, B, Table, rc.smem_twiddles, rc.persistent>(io, batch, s, nullptr);
             }
         });
     }
@@ -201,10 +222,10 @@ struct RowEngine {
             const auto* xz = reinterpret_cast<const float2*>(x);
             using PP = RowPlan<RowKind::R2c, M, true>;
             if constexpr (M >= 32 && PP::kPairLast) {
-                launch_rows<PP, false, B, Table, rc.smem_twiddles>(R2cPairIo{xz, y, keep}, batch, s, w);
+                launch_rows<PP, false, B, Table, rc.smem_twiddles, rc.persistent>(R2cPairIo{xz, y, keep}, batch, s, w);
             } else {
                 using PL = RowPlan<RowKind::R2c, M>;
-                launch_rows<PL, false, B, Table, rc.smem_twiddles>(R2cIo{xz, y, keep}, batch, s, w);
+                launch_rows<PL, false, B, Table, rc.smem_twiddles, rc.persistent>(R2cIo{xz, y, keep}, batch, s, w);
             }
         });
     }
@@ -222,9 +243,9 @@ struct RowEngine {
             const float2* w = row_half_turn<M, Table, rc.smem_twiddles>();
             auto* yz = reinterpret_cast<float2*>(y);
             if constexpr (M >= 32 && PL::kPairFirst) {
-                launch_rows<PL, true, B, Table, rc.smem_twiddles>(C2rPairIo{x, yz, keep, 1.0f / M}, batch, s, w);
+                launch_rows<PL, true, B, Table, rc.smem_twiddles, rc.persistent>(C2rPairIo{x, yz, keep, 1.0f / M}, batch, s, w);
             } else {
-                launch_rows<PL, true, B, Table, rc.smem_twiddles>(C2rIo{x, yz, keep, 1.0f / M}, batch, s, w);
+                launch_rows<PL, true, B, Table, rc.smem_twiddles, rc.persistent>(C2rIo{x, yz, keep, 1.0f / M}, batch, s, w);
             }
         });
     }

@@ -344,7 +344,7 @@ struct RowCtx {
     const float2* extra; // the Io's shared-memory table
 };
 
-template <class PL, bool Inv, int B, bool Table, class Io, bool TwGlobal = false>
+template <class PL, bool Inv, int B, bool Table, class Io, bool TwGlobal = false, bool Prefetch = false>
 __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
     row_kernel(const Io io, long long batch, const float2* __restrict__ tw_table,
                const float2* __restrict__ extra_table)
@@ -366,8 +366,7 @@ __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
 
     const int g = threadIdx.x / PL::P;
     const int t = threadIdx.x - g * PL::P;
-    for (long long tf0 = static_cast<long long>(blockIdx.x) * PL::G; tf0 < batch;
-         tf0 += static_cast<long long>(gridDim.x) * PL::G) {
+    auto context = [&](long long tf0) {
         RowCtx c;
         c.tf0 = tf0;
         c.count = static_cast<int>(batch - tf0 < PL::G ? batch - tf0 : PL::G);
@@ -378,11 +377,47 @@ __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
         c.buf = bufs + g * PL::BUF;
         c.bufs = bufs;
         c.extra = extra;
-
+        return c;
+    };
+    const long long stride = static_cast<long long>(gridDim.x) * PL::G;
+    if constexpr (Prefetch) {
+        // The next tile's loads are issued before this tile's passes, so they are in flight
+        // while it computes (for Io policies whose load is plain global loads).
+        long long tf0 = static_cast<long long>(blockIdx.x) * PL::G;
+        if (tf0 >= batch) {
+            return;
+        }
+        RowCtx c = context(tf0);
         float2 v[PL::E];
         io.template load<PL>(v, c);
-        run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
-        io.template store<PL, Inv>(v, c);
+        for (;;) {
+            const long long next = tf0 + stride;
+            const bool more = next < batch;
+            RowCtx cn = context(more ? next : tf0);
+            float2 vn[PL::E];
+            if (more) {
+                io.template load<PL>(vn, cn);
+            }
+            run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
+            io.template store<PL, Inv>(v, c);
+            if (!more) {
+                break;
+            }
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = vn[i];
+            }
+            c = cn;
+            tf0 = next;
+        }
+    } else {
+        for (long long tf0 = static_cast<long long>(blockIdx.x) * PL::G; tf0 < batch; tf0 += stride) {
+            const RowCtx c = context(tf0);
+            float2 v[PL::E];
+            io.template load<PL>(v, c);
+            run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
+            io.template store<PL, Inv>(v, c);
+        }
     }
 }
 

@@ -40,7 +40,9 @@ using PlanFor = Plan<N, default_e(N), false, default_threads(N)>;
 // whether the input is prefetched with bulk copies (the staged kernel), and whether the grid is
 // persistent (every resident slot once, walking the batch) or one CTA per tile of transforms
 // (no per-CTA set-up left once the tables are in global memory, and the hardware scheduler
-// balances the last wave: 1024-point complex transforms 47.3 -> 44.5 us). Each entry is the
+// balances the last wave: 1024-point complex transforms 47.3 -> 44.5 us), and whether the next
+// tile's input is loaded while this one computes (4096-point real forward 30.9 -> 28.8 us; the
+// inverse real and complex kernels measured slower with it). Each entry is the
 // best of a sweep on B200 at 2^24 points per call. The pattern: reading the twiddles from global
 // memory halves the shared memory of the real-transform kernels and lets the compiler hoist the
 // twiddle loads past the exchanges' barriers (1024 real points: 38.9 -> 30.0 us; 4096: 39.1 ->
@@ -56,6 +58,7 @@ struct RowChoice {
     bool smem_twiddles;
     bool staged;
     bool persistent;
+    bool prefetch;  // load the next tile while computing this one (plain-load inputs only)
 };
 
 __host__ __device__ constexpr RowChoice row_choice(RowKind k, int n)
@@ -75,7 +78,7 @@ __host__ __device__ constexpr RowChoice row_choice(RowKind k, int n)
          : n == 64     ? RowChoice{kMinThreads, 1, false, false, true}
          : n == 512    ? RowChoice{128, r2c ? 3 : 4, r2c, false, true}
          : n <= 1024   ? RowChoice{128, 4, false, false, true}
-         : n == 2048   ? RowChoice{128, r2c ? 4 : 6, false, false, r2c}
+         : n == 2048   ? RowChoice{128, r2c ? 5 : 6, false, false, r2c, r2c}
                        : RowChoice{kMinThreads, 2, false, false, true};
 }
 
@@ -121,13 +124,14 @@ const float2* row_half_turn()
     }
 }
 
-template <class PL, bool Inv, int B, bool Table, bool SmemTw, bool Persistent = true, class Io>
+template <class PL, bool Inv, int B, bool Table, bool SmemTw, bool Persistent = true,
+          bool Prefetch = false, class Io>
 void launch_rows(const Io& io, long long batch, cudaStream_t stream, const float2* extra_table)
 {
     if (batch <= 0) {
         return;
     }
-    auto kernel = row_kernel<PL, Inv, B, Table, Io, !SmemTw>;
+    auto kernel = row_kernel<PL, Inv, B, Table, Io, !SmemTw, Prefetch>;
     constexpr std::size_t smem = row_smem_bytes<PL, Io, !SmemTw>();
     static std::atomic<int> cache[kMaxDevices];
     const float2* tw = row_pass_table<PL, Table, SmemTw>();
@@ -222,10 +226,10 @@ struct RowEngine {
             const auto* xz = reinterpret_cast<const float2*>(x);
             using PP = RowPlan<RowKind::R2c, M, true>;
             if constexpr (M >= 32 && PP::kPairLast) {
-                launch_rows<PP, false, B, Table, rc.smem_twiddles, rc.persistent>(R2cPairIo{xz, y, keep}, batch, s, w);
+                launch_rows<PP, false, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(R2cPairIo{xz, y, keep}, batch, s, w);
             } else {
                 using PL = RowPlan<RowKind::R2c, M>;
-                launch_rows<PL, false, B, Table, rc.smem_twiddles, rc.persistent>(R2cIo{xz, y, keep}, batch, s, w);
+                launch_rows<PL, false, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(R2cIo{xz, y, keep}, batch, s, w);
             }
         });
     }

@@ -36,6 +36,8 @@
 #include "dft.cuh"
 #include "tma.cuh"
 
+#include <type_traits>
+
 namespace spectral::engine {
 
 constexpr int kMinThreads = 256;
@@ -332,6 +334,13 @@ __device__ __forceinline__ void run_passes(float2 (&v)[PL::E], int t, float2* bu
 // Loads and stores may stage through shared memory and use __syncthreads(): every thread of a
 // CTA runs the same number of iterations, inactive slots included.
 
+// Io policies that split their load into raw global loads (fetch) and arithmetic on them
+// (finish) declare kSplitLoad = true.
+template <class Io, class = void>
+struct split_load : std::false_type {};
+template <class Io>
+struct split_load<Io, std::void_t<decltype(Io::kSplitLoad)>> : std::bool_constant<Io::kSplitLoad> {};
+
 struct RowCtx {
     long long tf;        // this slot's transform (valid only when `active`)
     long long tf0;       // the CTA's first transform in this iteration
@@ -380,7 +389,34 @@ __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
         return c;
     };
     const long long stride = static_cast<long long>(gridDim.x) * PL::G;
-    if constexpr (Prefetch) {
+    if constexpr (Prefetch && split_load<Io>::value) {
+        // The next tile's raw loads are issued before this tile's passes; the Io's arithmetic on
+        // them (finish) waits for the next iteration.
+        long long tf0 = static_cast<long long>(blockIdx.x) * PL::G;
+        if (tf0 >= batch) {
+            return;
+        }
+        RowCtx c = context(tf0);
+        float2 raw[PL::E + 1];
+        io.template fetch<PL>(raw, c);
+        for (;;) {
+            const long long next = tf0 + stride;
+            const bool more = next < batch;
+            float2 v[PL::E];
+            io.template finish<PL>(v, raw, c);
+            const RowCtx cn = context(more ? next : tf0);
+            if (more) {
+                io.template fetch<PL>(raw, cn);
+            }
+            run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
+            io.template store<PL, Inv>(v, c);
+            if (!more) {
+                break;
+            }
+            c = cn;
+            tf0 = next;
+        }
+    } else if constexpr (Prefetch) {
         // The next tile's loads are issued before this tile's passes, so they are in flight
         // while it computes (for Io policies whose load is plain global loads).
         long long tf0 = static_cast<long long>(blockIdx.x) * PL::G;
@@ -980,22 +1016,36 @@ struct C2rPairIo {
     template <class PL, bool Table>
     __device__ static void prologue(float2* w, const float2* table) { fill_half_turn<PL, Table>(w, table); }
 
+    // The prepare step in two halves: gather the inputs of the thread's two mirrored butterflies
+    // (raw[0 .. R-1] and raw[R .. 2R-1]; raw[2R] = X[N] for thread 0), then combine them. Split,
+    // the gather of the next tile can be issued before this tile's passes (kSplitLoad).
+    static constexpr bool kSplitLoad = true;
+
     template <class PL, class Get>
-    __device__ __forceinline__ void prepare(float2 (&v)[PL::E], const RowCtx& c, Get&& get) const
+    __device__ __forceinline__ void gather(float2 (&raw)[PL::E + 1], const RowCtx& c, Get&& get) const
     {
         static_assert(PL::kPairFirst, "needs two butterflies per thread in the first pass");
+        constexpr int R = PL::radix(0);
+        constexpr int NB = PL::N / R;  // = 2P
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            raw[r] = get(butterfly<true, PL::P>(c.t, 0) + r * NB);
+            raw[R + r] = get(butterfly<true, PL::P>(c.t, 1) + r * NB);
+        }
+        raw[2 * R] = c.t == 0 ? get(PL::N) : make_float2(0.0f, 0.0f);
+    }
+
+    template <class PL>
+    __device__ __forceinline__ void combine(float2 (&v)[PL::E], const float2 (&raw)[PL::E + 1],
+                                            const RowCtx& c) const
+    {
         constexpr int N = PL::N;
         constexpr int P = PL::P;
         constexpr int R = PL::radix(0);
         constexpr int NB = N / R;  // = 2P
         const int t = c.t;
-        float2 a[R];
-        float2 b[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            a[r] = get(butterfly<true, P>(t, 0) + r * NB);
-            b[r] = get(butterfly<true, P>(t, 1) + r * NB);
-        }
+        const float2* a = raw;
+        const float2* b = raw + R;
         if (t != 0) {
 #pragma unroll
             for (int r = 0; r < R; ++r) {
@@ -1004,7 +1054,7 @@ struct C2rPairIo {
             }
         } else {
             float2 unused;
-            c2r_pair(0, a[0], get(N), c.extra[0], v[0], unused);
+            c2r_pair(0, a[0], raw[2 * R], c.extra[0], v[0], unused);
 #pragma unroll
             for (int r = 1; r <= R / 2; ++r) {
                 c2r_pair(r * NB, a[r], a[R - r], c.extra[r * NB], v[2 * r], v[2 * (R - r)]);
@@ -1015,6 +1065,43 @@ struct C2rPairIo {
                          v[1 + 2 * (R - 1 - r)]);
             }
         }
+    }
+
+    template <class PL, class Get>
+    __device__ __forceinline__ void prepare(float2 (&v)[PL::E], const RowCtx& c, Get&& get) const
+    {
+        float2 raw[PL::E + 1];
+        gather<PL>(raw, c, get);
+        combine<PL>(v, raw, c);
+    }
+
+    template <class PL>
+    __device__ __forceinline__ void fetch(float2 (&raw)[PL::E + 1], const RowCtx& c) const
+    {
+        if (!c.active) {
+#pragma unroll
+            for (int i = 0; i <= PL::E; ++i) {
+                raw[i] = make_float2(0.0f, 0.0f);
+            }
+            return;
+        }
+        const float2* row = x + c.tf * keep;
+        const int kp = keep;
+        gather<PL>(raw, c, [&](int k) { return k < kp ? __ldg(row + k) : make_float2(0.0f, 0.0f); });
+    }
+
+    template <class PL>
+    __device__ __forceinline__ void finish(float2 (&v)[PL::E], const float2 (&raw)[PL::E + 1],
+                                           const RowCtx& c) const
+    {
+        if (!c.active) {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = make_float2(0.0f, 0.0f);
+            }
+            return;
+        }
+        combine<PL>(v, raw, c);
     }
 
     template <class PL>

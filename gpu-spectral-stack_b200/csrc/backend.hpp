@@ -38,14 +38,6 @@ struct Backend {
                         long long fields, cudaStream_t s);
     void (*irfft2_modes)(const float2* modes, float* y, int n1, int n2, int m1, int m2,
                          long long fields, cudaStream_t s);
-    // Whole 2D real transforms in one kernel per direction (fields.cuh) for the shapes
-    // `fields_supported` accepts, with n1 (n2/2) complex values of scratch per field;
-    // nullptr when there are none. irfft2 divides by n1 n2.
-    bool (*fields_supported)(int n1, int n2);
-    void (*rfft2_fields)(const float* x, float2* y, float2* scratch, int n1, int n2, long long fields,
-                         cudaStream_t s);
-    void (*irfft2_fields)(const float2* y, float* x, float2* scratch, int n1, int n2, long long fields,
-                          cudaStream_t s);
 };
 
 // The register engine in its four registry variants (variant_*.cu) and the simple reference-

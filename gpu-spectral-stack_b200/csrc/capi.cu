@@ -209,19 +209,8 @@ std::size_t fft2_c2c_work(const Impl&, Columns columns, int n1, int n2, long lon
     return columns == Columns::Strided ? 0 : 2 * count3(batch, n1, n2);
 }
 
-// The whole-field kernel serves the strided method where the shape allows it; its scratch is
-// n1 (n2/2) complex values per field.
-bool fields_path(const Impl& impl, Columns columns, int n1, int n2)
-{
-    return columns == Columns::Strided && impl.backend->fields_supported != nullptr
-           && impl.backend->fields_supported(n1, n2);
-}
-
 std::size_t fft2_r2c_work(const Impl& impl, Columns columns, int n1, int n2, long long batch)
 {
-    if (fields_path(impl, columns, n1, n2)) {
-        return count3(batch, n1, n2 / 2);
-    }
     const std::size_t half = columns == Columns::Strided ? 0 : 2 * count3(batch, n1, n2 / 2 + 1);
     return half + real_work(impl, n1, n2, batch);
 }
@@ -252,10 +241,6 @@ void fft2_r2c(const Impl& impl, Columns columns, const float* x, float2* y, int 
               long long batch, float2* work, cudaStream_t s)
 {
     const int w = n2 / 2 + 1;
-    if (fields_path(impl, columns, n1, n2)) {
-        impl.backend->rfft2_fields(x, y, work, n1, n2, batch, s);
-        return;
-    }
     if (columns == Columns::Strided) {
         impl.backend->r2c(x, y, n2, batch * n1, w, work, s);
         columns_any(impl, y, y, n1, w, batch, 0, 0, Direction::Forward, s);
@@ -275,10 +260,6 @@ void fft2_c2r(const Impl& impl, Columns columns, const float2* x, float* y, int 
 {
     const int w = n2 / 2 + 1;
     const std::size_t q = count3(batch, n1, w);
-    if (fields_path(impl, columns, n1, n2)) {
-        impl.backend->irfft2_fields(x, y, work, n1, n2, batch, s);  // needs n1 (n2/2) per field
-        return;
-    }
     if (columns == Columns::Strided) {
         // Columns first, out of place (the input is not ours to overwrite), then rows.
         float2* a = work;

@@ -33,6 +33,6 @@ void c2r(const float2* x, float* y, int n, long long batch, int keep, float2* wo
 
 }  // namespace
 
-const Backend kNaive = {&c2c, &r2c, &c2r, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+const Backend kNaive = {&c2c, &r2c, &c2r, nullptr, nullptr, nullptr, nullptr};
 
 }  // namespace spectral

@@ -3,7 +3,6 @@
 // variants compile in parallel.
 
 #include "backend.hpp"
-#include "fields.cuh"
 #include "pruned2d.cuh"
 
 namespace spectral {
@@ -12,19 +11,6 @@ namespace {
 using Rows = engine::RowEngine<8, false>;
 using Cols = engine::ColumnEngine<8, false>;
 using Fused = engine::Pruned2dEngine<8, false>;
-using Whole = engine::FieldsEngine<8, false>;
-
-void rfft2_fields(const float* x, float2* y, float2* scratch, int n1, int n2, long long fields,
-                  cudaStream_t s)
-{
-    Whole::run<true>(reinterpret_cast<const float2*>(x), y, scratch, n1, n2, fields, s);
-}
-
-void irfft2_fields(const float2* y, float* x, float2* scratch, int n1, int n2, long long fields,
-                   cudaStream_t s)
-{
-    Whole::run<false>(y, reinterpret_cast<float2*>(x), scratch, n1, n2, fields, s);
-}
 
 void c2c(const float2* x, float2* y, int n, long long batch, Direction d, int keep, cudaStream_t s)
 {
@@ -38,7 +24,6 @@ void c2c(const float2* x, float2* y, int n, long long batch, Direction d, int ke
 }  // namespace
 
 const Backend kEngineR8 = {&c2c, &Rows::r2c, &Rows::c2r, &Cols::columns, &Fused::supported,
-                      &Fused::forward, &Fused::inverse,
-                      &Whole::supported, &rfft2_fields, &irfft2_fields};
+                      &Fused::forward, &Fused::inverse};
 
 }  // namespace spectral

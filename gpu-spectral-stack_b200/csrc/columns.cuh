@@ -36,15 +36,19 @@ struct ColumnCtx {
     float2* tile;
 };
 
-template <class PL, int C, bool Inv, int B, bool Table, class Io>
-__global__ void __launch_bounds__(C * PL::P)
+template <class PL, int C, bool Inv, int B, bool Table, class Io, bool TwGlobal = false>
+__global__ void __launch_bounds__(C * PL::P, PL::MIN_BLOCKS)
     column_kernel(const Io io, long long transforms, const float2* __restrict__ tw_table)
 {
     extern __shared__ float4 smem_raw[];
-    float2* tw = reinterpret_cast<float2*>(smem_raw);
-    float2* tile = tw + ((PL::TW + 1) & ~1);
+    // TwGlobal: the pass tables are read where they lie in global memory (L1-resident).
+    float2* tw_s = reinterpret_cast<float2*>(smem_raw);
+    float2* tile = tw_s + (TwGlobal ? 0 : ((PL::TW + 1) & ~1));
+    const float2* tw = TwGlobal ? tw_table : tw_s;
 
-    fill_pass_twiddles<PL, Table>(tw, tw_table);
+    if constexpr (!TwGlobal) {
+        fill_pass_twiddles<PL, Table>(tw_s, tw_table);
+    }
     __syncthreads();
 
     const int c = threadIdx.x % C;
@@ -66,11 +70,12 @@ __global__ void __launch_bounds__(C * PL::P)
     }
 }
 
-template <class PL, int C>
+template <class PL, int C, bool TwGlobal = false>
 constexpr std::size_t column_smem_bytes()
 {
     return sizeof(float2)
-           * (static_cast<std::size_t>((PL::TW + 1) & ~1) + static_cast<std::size_t>(C) * (PL::N + 1));
+           * ((TwGlobal ? 0 : static_cast<std::size_t>((PL::TW + 1) & ~1))
+              + static_cast<std::size_t>(C) * (PL::N + 1));
 }
 
 template <class PL, bool Inv, int B, bool Table, class Io>
@@ -112,47 +117,79 @@ struct StridedIo {
     int m1_out;
     float scale;
 
+    // Array and column of column f: one division per tile, in 32 bits where f allows.
+    __device__ __forceinline__ void locate(long long f, long long& slab, int& col) const
+    {
+        if (f < (1LL << 31)) {
+            const unsigned q = static_cast<unsigned>(f) / static_cast<unsigned>(cols);
+            slab = q;
+            col = static_cast<int>(static_cast<unsigned>(f) - q * static_cast<unsigned>(cols));
+        } else {
+            slab = f / cols;
+            col = static_cast<int>(f - slab * cols);
+        }
+    }
+
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], const ColumnCtx& c) const
     {
-        const long long f = c.f;
-        const int t = c.t;
+        const float2 zero = make_float2(0.0f, 0.0f);
         if (!c.active) {
 #pragma unroll
             for (int i = 0; i < PL::E; ++i) {
-                v[i] = make_float2(0.0f, 0.0f);
+                v[i] = zero;
             }
             return;
         }
-        const long long slab = f / cols;
-        const long long col = f - slab * cols;
+        long long slab = 0;
+        int col = 0;
+        locate(c.f, slab, col);
         const int rows = m1_in > 0 ? 2 * m1_in : PL::N;
         const float2* base = x + slab * rows * cols + col;
+        // Plain loads: the column transforms may run in place (x == y).
+        if (m1_in == 0) {
+            const float2* p = base + static_cast<long long>(c.t) * cols;
+            const long long step = static_cast<long long>(PL::P) * cols;
 #pragma unroll
-        for (int i = 0; i < PL::E; ++i) {
-            const int row = mode_row(t + i * PL::P, PL::N, m1_in);
-            // Plain loads: the column transforms may run in place (x == y).
-            v[i] = row >= 0 ? base[static_cast<long long>(row) * cols] : make_float2(0.0f, 0.0f);
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = *p;
+                p += step;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                const int row = mode_row(c.t + i * PL::P, PL::N, m1_in);
+                v[i] = row >= 0 ? base[static_cast<long long>(row) * cols] : zero;
+            }
         }
     }
 
     template <class PL, int C, bool Inv>
     __device__ __forceinline__ void store(float2 (&v)[PL::E], const ColumnCtx& c) const
     {
-        const long long f = c.f;
-        const int t = c.t;
         if (!c.active) {
             return;
         }
-        const long long slab = f / cols;
-        const long long col = f - slab * cols;
+        long long slab = 0;
+        int col = 0;
+        locate(c.f, slab, col);
         const int rows = m1_out > 0 ? 2 * m1_out : PL::N;
         float2* base = y + slab * rows * cols + col;
+        if (m1_out == 0) {
+            float2* p = base + static_cast<long long>(c.t) * cols;
+            const long long step = static_cast<long long>(PL::P) * cols;
 #pragma unroll
-        for (int i = 0; i < PL::E; ++i) {
-            const int row = mode_row(t + i * PL::P, PL::N, m1_out);
-            if (row >= 0) {
-                base[static_cast<long long>(row) * cols] = Inv ? cscale(v[i], scale) : v[i];
+            for (int i = 0; i < PL::E; ++i) {
+                *p = Inv ? cscale(v[i], scale) : v[i];
+                p += step;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                const int row = mode_row(c.t + i * PL::P, PL::N, m1_out);
+                if (row >= 0) {
+                    base[static_cast<long long>(row) * cols] = Inv ? cscale(v[i], scale) : v[i];
+                }
             }
         }
     }
@@ -225,6 +262,14 @@ struct FourStepIo {
     }
 };
 
+// Strided column plans with the CTAs per SM that the register budget must allow, from a sweep
+// on B200 (256-point columns of 256 fields x 129: 32.3 us at the compiler's own budget, two CTAs
+// per SM; 29.7 us at three; 512-point columns 41.1 -> 38.8 us at two).
+__host__ __device__ constexpr int column_min_blocks(int n) { return n == 256 ? 3 : n == 512 ? 2 : 1; }
+
+template <int N>
+using ColumnPlan = Plan<N, default_e(N), false, default_threads(N), column_min_blocks(N)>;
+
 template <int B, bool Table>
 struct ColumnEngine {
     static void columns(const float2* x, float2* y, int n, int cols, long long slabs, int m1_in,
@@ -232,7 +277,7 @@ struct ColumnEngine {
     {
         dispatch_pow2<2, kMaxRowN>(n, [&](auto n_) {
             constexpr int N = decltype(n_)::value;
-            using PL = PlanFor<N>;
+            using PL = ColumnPlan<N>;
             const long long transforms = slabs * cols;
             if (d == Direction::Forward) {
                 launch_columns<PL, false, B, Table>(StridedIo{x, y, cols, m1_in, m1_out, 1.0f},

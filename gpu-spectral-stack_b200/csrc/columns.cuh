@@ -40,6 +40,8 @@ template <class PL, int C, bool Inv, int B, bool Table, class Io, bool TwGlobal 
 __global__ void __launch_bounds__(C * PL::P, PL::MIN_BLOCKS)
     column_kernel(const Io io, long long transforms, const float2* __restrict__ tw_table)
 {
+    wait_for_previous_grid();
+    allow_next_grid();
     extern __shared__ float4 smem_raw[];
     // TwGlobal: the pass tables are read where they lie in global memory (L1-resident).
     float2* tw_s = reinterpret_cast<float2*>(smem_raw);
@@ -91,8 +93,7 @@ void launch_columns(const Io& io, long long transforms, cudaStream_t stream)
     const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E) : nullptr;
     const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), C * PL::P, smem,
                                           cache, (transforms + C - 1) / C);
-    kernel<<<grid, C * PL::P, smem, stream>>>(io, transforms, tw);
-    SPECTRAL_CUDA(cudaGetLastError());
+    launch_pdl(kernel, grid, C * PL::P, smem, stream, io, transforms, tw);
 }
 
 // Where frequency `pos` of an N-point column is stored when only the 2 m1 lowest frequencies

@@ -353,11 +353,28 @@ struct RowCtx {
     const float2* extra; // the Io's shared-memory table
 };
 
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization
+// attribute may start while the previous kernel on its stream drains; it waits here, before its
+// first global access, until that kernel has completed and its writes are visible. Launched
+// without the attribute, the wait returns at once.
+__device__ __forceinline__ void wait_for_previous_grid()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next kernel on the stream begin launching (it still waits for this one to complete).
+__device__ __forceinline__ void allow_next_grid()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 template <class PL, bool Inv, int B, bool Table, class Io, bool TwGlobal = false, bool Prefetch = false>
 __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
     row_kernel(const Io io, long long batch, const float2* __restrict__ tw_table,
                const float2* __restrict__ extra_table)
 {
+    wait_for_previous_grid();
+    allow_next_grid();
     extern __shared__ float4 smem_raw[];
     // TwGlobal: the tables are read where they lie in global memory (one L1-resident copy per SM
     // instead of one shared-memory copy per CTA, so more CTAs fit).
@@ -487,6 +504,8 @@ __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
     staged_row_kernel(const Io io, long long batch, const float2* __restrict__ tw_table,
                       const float2* __restrict__ extra_table, unsigned* fault)
 {
+    wait_for_previous_grid();
+    allow_next_grid();
     extern __shared__ float4 smem_raw[];
     constexpr int kExtra = TwGlobal ? 0 : (Io::template extra<PL>() + 1) & ~1;
     constexpr int kTw = TwGlobal ? 0 : (PL::TW + 1) & ~1;

@@ -64,4 +64,26 @@ inline unsigned persistent_grid(const void* kernel, int threads, std::size_t sme
     return static_cast<unsigned>(grid < 1 ? 1 : grid);
 }
 
+// Launches `kernel` with programmatic dependent launch allowed: it may be scheduled while the
+// previous kernel on the stream drains, which hides the launch gap between back-to-back
+// transforms. The kernel must call griddepcontrol.wait (engine.cuh: wait_for_previous_grid)
+// before its first global memory access; launched after a kernel that does not trigger early,
+// that wait simply lasts until the previous kernel completes.
+template <class... KArgs, class... Args>
+void launch_pdl(void (*kernel)(KArgs...), unsigned grid, int threads, std::size_t smem,
+                cudaStream_t stream, Args&&... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SPECTRAL_CUDA(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...));
+}
+
 }  // namespace spectral

@@ -93,7 +93,7 @@ void launch_columns(const Io& io, long long transforms, cudaStream_t stream)
     const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E) : nullptr;
     const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), C * PL::P, smem,
                                           cache, (transforms + C - 1) / C);
-    launch_pdl(kernel, grid, C * PL::P, smem, stream, io, transforms, tw);
+    launch_pdl(kernel, grid, static_cast<unsigned>(C * PL::P), smem, stream, io, transforms, tw);
 }
 
 // Where frequency `pos` of an N-point column is stored when only the 2 m1 lowest frequencies

@@ -72,6 +72,21 @@ __device__ __forceinline__ float2 csub(float2 a, float2 b)
 {
     return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a);
 }
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization
+// attribute may start while the previous kernel on its stream drains; it waits here, before its
+// first global access, until that kernel has completed and its writes are visible. Launched
+// without the attribute, the wait returns at once.
+__device__ __forceinline__ void wait_for_previous_grid()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next kernel on the stream begin launching (it still waits for this one to complete).
+__device__ __forceinline__ void allow_next_grid()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float2 cscale(float2 a, float s) { return __fmul2_rn(a, make_float2(s, s)); }
 
 // a * w for the forward transform, a * conj(w) for the inverse: twiddle tables hold the forward

@@ -14,6 +14,7 @@
 #include "../../include/spectral_b200.h"
 
 #include "backend.hpp"
+#include "launch.cuh"
 
 #include <string>
 
@@ -29,6 +30,8 @@ __global__ void __launch_bounds__(kModesPerCta * kWarps, 2)
     contract_kernel(const float2* __restrict__ x, const float2* __restrict__ w,
                     float2* __restrict__ out, int batch, int cin, int cout, long long modes)
 {
+    wait_for_previous_grid();
+    allow_next_grid();
     const long long m = static_cast<long long>(blockIdx.x) * kModesPerCta + (threadIdx.x & 31);
     const int warp = threadIdx.x >> 5;
     const int b0 = blockIdx.y * kBatchPerThread;
@@ -103,12 +106,12 @@ extern "C" int spectral_mode_contract(const void* x, const void* w, void* out, l
         set_last_error("mode_contract: batch or cout too large for one launch");
         return SPECTRAL_INVALID_ARGUMENT;
     }
-    contract_kernel<<<grid, kModesPerCta * kWarps, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const float2*>(x), static_cast<const float2*>(w), static_cast<float2*>(out),
-        static_cast<int>(batch), cin, cout, modes);
-    const cudaError_t err = cudaGetLastError();
-    if (err != cudaSuccess) {
-        set_last_error(std::string("CUDA error: ") + cudaGetErrorString(err));
+    try {
+        launch_pdl(contract_kernel, grid, dim3(kModesPerCta * kWarps), 0, static_cast<cudaStream_t>(stream),
+                   static_cast<const float2*>(x), static_cast<const float2*>(w), static_cast<float2*>(out),
+                   static_cast<int>(batch), cin, cout, modes);
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
         return SPECTRAL_CUDA_ERROR;
     }
     return SPECTRAL_OK;

@@ -353,21 +353,6 @@ struct RowCtx {
     const float2* extra; // the Io's shared-memory table
 };
 
-// Programmatic dependent launch: a kernel launched with the programmatic-serialization
-// attribute may start while the previous kernel on its stream drains; it waits here, before its
-// first global access, until that kernel has completed and its writes are visible. Launched
-// without the attribute, the wait returns at once.
-__device__ __forceinline__ void wait_for_previous_grid()
-{
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-// Lets the next kernel on the stream begin launching (it still waits for this one to complete).
-__device__ __forceinline__ void allow_next_grid()
-{
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 template <class PL, bool Inv, int B, bool Table, class Io, bool TwGlobal = false, bool Prefetch = false>
 __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
     row_kernel(const Io io, long long batch, const float2* __restrict__ tw_table,

@@ -70,15 +70,15 @@ inline unsigned persistent_grid(const void* kernel, int threads, std::size_t sme
 // before its first global memory access; launched after a kernel that does not trigger early,
 // that wait simply lasts until the previous kernel completes.
 template <class... KArgs, class... Args>
-void launch_pdl(void (*kernel)(KArgs...), unsigned grid, int threads, std::size_t smem,
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, std::size_t smem,
                 cudaStream_t stream, Args&&... args)
 {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;

@@ -67,6 +67,8 @@ __global__ void __launch_bounds__(256)
                      int m1, int m2, const float2* __restrict__ twr_g,
                      const float2* __restrict__ half_g, const float2* __restrict__ twc_g)
 {
+    wait_for_previous_grid();
+    allow_next_grid();
     using K = Pruned2d<N1, N2, B, Table>;
     using RP = typename K::RP;
     using CP = typename K::CP;
@@ -152,6 +154,8 @@ __global__ void __launch_bounds__(256)
                      int m1, int m2, const float2* __restrict__ twr_g,
                      const float2* __restrict__ half_g, const float2* __restrict__ twc_g)
 {
+    wait_for_previous_grid();
+    allow_next_grid();
     using K = Pruned2d<N1, N2, B, Table>;
     using RP = typename K::RP;
     using CP = typename K::CP;
@@ -257,8 +261,7 @@ struct Pruned2dEngine {
                 const float2* twc = Table ? twiddles::pass_table(N1, K::CP::E) : nullptr;
                 const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel),
                                                       K::THREADS, K::kSmem, cache, fields);
-                kernel<<<grid, K::THREADS, K::kSmem, stream>>>(in, out, fields, m1, m2, twr, half, twc);
-                SPECTRAL_CUDA(cudaGetLastError());
+                launch_pdl(kernel, grid, static_cast<unsigned>(K::THREADS), K::kSmem, stream, in, out, fields, m1, m2, twr, half, twc);
             });
         });
     }

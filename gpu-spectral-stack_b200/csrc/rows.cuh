@@ -139,7 +139,7 @@ void launch_rows(const Io& io, long long batch, cudaStream_t stream, const float
     const float2* tw = row_pass_table<PL, Table, SmemTw>();
     const unsigned grid = row_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem, cache,
                                    (batch + PL::G - 1) / PL::G, Persistent);
-    launch_pdl(kernel, grid, PL::THREADS, smem, stream, io, batch, tw, extra_table);
+    launch_pdl(kernel, grid, static_cast<unsigned>(PL::THREADS), smem, stream, io, batch, tw, extra_table);
 }
 
 // The staged kernel (bulk-copy prefetch, engine.cuh), when the input satisfies cp.async.bulk's
@@ -159,7 +159,7 @@ void launch_rows_staged(const Io& io, long long batch, cudaStream_t stream, cons
     const float2* tw = row_pass_table<PL, Table, SmemTw>();
     const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS, smem,
                                           cache, (batch + PL::G - 1) / PL::G);
-    launch_pdl(kernel, grid, PL::THREADS, smem, stream, io, batch, tw, extra_table, device_fault_word());
+    launch_pdl(kernel, grid, static_cast<unsigned>(PL::THREADS), smem, stream, io, batch, tw, extra_table, device_fault_word());
 }
 
 // Calls f(std::integral_constant<int, n>) for a power of two n in [Lo, Hi], else throws.

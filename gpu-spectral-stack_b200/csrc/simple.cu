@@ -39,6 +39,8 @@ constexpr int kTileRows = 8;
 __global__ void transpose_kernel(const float2* __restrict__ x, float2* __restrict__ y, int rows,
                                  int cols, long long batch)
 {
+    wait_for_previous_grid();
+    allow_next_grid();
     __shared__ float2 tile[kTile][kTile + 1];
     const long long size = static_cast<long long>(rows) * cols;
     for (long long b = blockIdx.z; b < batch; b += gridDim.z) {
@@ -195,8 +197,7 @@ void transpose(const float2* x, float2* y, int rows, int cols, long long batch, 
     const dim3 grid(static_cast<unsigned>((cols + kTile - 1) / kTile),
                     static_cast<unsigned>((rows + kTile - 1) / kTile),
                     static_cast<unsigned>(std::min(batch, 65535LL)));
-    transpose_kernel<<<grid, block, 0, s>>>(x, y, rows, cols, batch);
-    SPECTRAL_CUDA(cudaGetLastError());
+    launch_pdl(transpose_kernel, grid, block, 0, s, x, y, rows, cols, batch);
 }
 
 void gather_modes(const float2* full, float2* modes, int n1, int w, int m1, int m2, long long batch,

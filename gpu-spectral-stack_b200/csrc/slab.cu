@@ -142,6 +142,8 @@ template <class PL, bool Inv, class Io>
 __global__ void __launch_bounds__(PL::THREADS)
     slab_row_kernel(const Io io, const float2* __restrict__ tw)
 {
+    wait_for_previous_grid();
+    allow_next_grid();
     extern __shared__ float4 smem_raw[];
     float2* bufs = reinterpret_cast<float2*>(smem_raw);
     const int g = threadIdx.x / PL::P;
@@ -183,8 +185,7 @@ void slab_rows(int n, long long rows, cudaStream_t s, MakeIo&& make_io)
         const float2* tw = twiddles::pass_table(PL::N, PL::E);
         const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS,
                                               smem, cache, (rows + PL::G - 1) / PL::G);
-        kernel<<<grid, PL::THREADS, smem, s>>>(io, tw);
-        SPECTRAL_CUDA(cudaGetLastError());
+        launch_pdl(kernel, grid, static_cast<unsigned>(PL::THREADS), smem, s, io, tw);
     });
 }
 

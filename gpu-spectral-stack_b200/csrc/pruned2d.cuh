@@ -16,12 +16,12 @@
 
 namespace spectral::engine {
 
-template <int N1, int N2, int B, bool Table>
+template <int N1, int N2, int B, bool Table, int T = 256>
 struct Pruned2d {
     static constexpr int M = N2 / 2;  // packed complex points per row
     using RP = PlanFor<M>;
     using CP = PlanFor<N1>;
-    static constexpr int THREADS = 256;
+    static constexpr int THREADS = T;
     static_assert(RP::P <= THREADS && CP::P <= THREADS, "field too large for one CTA");
     static constexpr int RG = THREADS / RP::P;  // rows in flight
     static constexpr int CW = THREADS / CP::P;  // columns in flight: the largest m2 supported
@@ -61,15 +61,15 @@ struct Pruned2d {
     }
 };
 
-template <int N1, int N2, int B, bool Table>
-__global__ void __launch_bounds__(256)
+template <int N1, int N2, int B, bool Table, int T>
+__global__ void __launch_bounds__(T)
     pruned2d_forward(const float2* __restrict__ x, float2* __restrict__ modes, long long fields,
                      int m1, int m2, const float2* __restrict__ twr_g,
                      const float2* __restrict__ half_g, const float2* __restrict__ twc_g)
 {
     wait_for_previous_grid();
     allow_next_grid();
-    using K = Pruned2d<N1, N2, B, Table>;
+    using K = Pruned2d<N1, N2, B, Table, T>;
     using RP = typename K::RP;
     using CP = typename K::CP;
     constexpr int M = K::M;
@@ -148,15 +148,15 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-template <int N1, int N2, int B, bool Table>
-__global__ void __launch_bounds__(256)
+template <int N1, int N2, int B, bool Table, int T>
+__global__ void __launch_bounds__(T)
     pruned2d_inverse(const float2* __restrict__ modes, float2* __restrict__ y, long long fields,
                      int m1, int m2, const float2* __restrict__ twr_g,
                      const float2* __restrict__ half_g, const float2* __restrict__ twc_g)
 {
     wait_for_previous_grid();
     allow_next_grid();
-    using K = Pruned2d<N1, N2, B, Table>;
+    using K = Pruned2d<N1, N2, B, Table, T>;
     using RP = typename K::RP;
     using CP = typename K::CP;
     constexpr int M = K::M;
@@ -245,6 +245,21 @@ struct Pruned2dEngine {
         return ok;
     }
 
+    template <int N1, int N2, int T, bool Forward>
+    static void launch(const float2* in, float2* out, int m1, int m2, long long fields, cudaStream_t stream)
+    {
+        using K = Pruned2d<N1, N2, B, Table, T>;
+        auto kernel = Forward ? pruned2d_forward<N1, N2, B, Table, T> : pruned2d_inverse<N1, N2, B, Table, T>;
+        static std::atomic<int> cache[kMaxDevices];
+        const float2* twr = Table ? twiddles::pass_table(K::M, K::RP::E) : nullptr;
+        const float2* half = Table ? twiddles::half_turn(K::M) : nullptr;
+        const float2* twc = Table ? twiddles::pass_table(N1, K::CP::E) : nullptr;
+        const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), K::THREADS,
+                                              K::kSmem, cache, fields);
+        launch_pdl(kernel, grid, static_cast<unsigned>(K::THREADS), K::kSmem, stream, in, out, fields,
+                   m1, m2, twr, half, twc);
+    }
+
     template <bool Forward>
     static void run(const float2* in, float2* out, int n1, int n2, int m1, int m2, long long fields,
                     cudaStream_t stream)
@@ -253,15 +268,13 @@ struct Pruned2dEngine {
             dispatch_pow2<kMin, kMax>(n2, [&](auto n2_) {
                 constexpr int N1 = decltype(n1_)::value;
                 constexpr int N2 = decltype(n2_)::value;
-                using K = Pruned2d<N1, N2, B, Table>;
-                auto kernel = Forward ? pruned2d_forward<N1, N2, B, Table> : pruned2d_inverse<N1, N2, B, Table>;
-                static std::atomic<int> cache[kMaxDevices];
-                const float2* twr = Table ? twiddles::pass_table(K::M, K::RP::E) : nullptr;
-                const float2* half = Table ? twiddles::half_turn(K::M) : nullptr;
-                const float2* twc = Table ? twiddles::pass_table(N1, K::CP::E) : nullptr;
-                const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel),
-                                                      K::THREADS, K::kSmem, cache, fields);
-                launch_pdl(kernel, grid, static_cast<unsigned>(K::THREADS), K::kSmem, stream, in, out, fields, m1, m2, twr, half, twc);
+                // 128-thread CTAs hold half the columns in flight: where the kept columns fit,
+                // the column stage computes no discarded columns and twice the CTAs fit per SM.
+                if (m2 <= Pruned2d<N1, N2, B, Table, 128>::CW) {
+                    launch<N1, N2, 128, Forward>(in, out, m1, m2, fields, stream);
+                } else {
+                    launch<N1, N2, 256, Forward>(in, out, m1, m2, fields, stream);
+                }
             });
         });
     }

@@ -15,6 +15,7 @@ except ImportError as exc:  # pragma: no cover - exercised only on an unbuilt ch
         "spectral/libspectral_b200.so); run `python gpu-spectral-stack_b200/build.py`"
     ) from exc
 
+from . import nn
 from .ops import (
     FFT_IMPLS,
     fft2,

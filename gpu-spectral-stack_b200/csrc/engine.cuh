@@ -110,13 +110,21 @@ struct Plan {
     {
         return span(s) < 16 ? p + span(s) * (p / (span(s) * radix(s))) : p;
     }
+    // Slot length. The exchange accesses of one transform's P threads touch 2 P consecutive
+    // banks (8-byte values); when P < 16, 32 / P transforms share a warp, and a slot length of
+    // P (mod 16) places transform g's accesses at bank 2 P g (mod 32): the transforms of each
+    // half-warp take disjoint banks. P = 1 makes it odd, which also lets 16 consecutive slots'
+    // same position (the [slot][position] staging reads) fall on distinct banks.
     __host__ __device__ static constexpr int buffer_entries()
     {
         int b = N + 1;
         for (int s = 0; s + 1 < PASSES; ++s) {
             b = cmax(b, pad(N - 1, s) + 1);
         }
-        return b | 1;  // odd: a column of the [slot][position] staging layout spans all banks
+        if (P < 16) {
+            return b + ((P - b % 16) % 16 + 16) % 16;
+        }
+        return b | 1;
     }
     static constexpr int BUF = buffer_entries();  // per-transform slot in shared memory
 };

@@ -25,12 +25,15 @@ struct Pruned2d {
     static_assert(RP::P <= THREADS && CP::P <= THREADS, "field too large for one CTA");
     static constexpr int RG = THREADS / RP::P;  // rows in flight
     static constexpr int CW = THREADS / CP::P;  // columns in flight: the largest m2 supported
+    // Row stride of the [row][column] tile: CW, plus 8 entries when CW rows are whole 128-byte
+    // lines, so the rows that one warp's row stage writes at once alternate bank halves.
+    static constexpr int CS = CW % 16 == 0 ? CW + 8 : CW;
 
     static constexpr int kTwR = (RP::TW + 1) & ~1;
     static constexpr int kHalf = (M + 2) & ~1;
     static constexpr int kTwC = (CP::TW + 1) & ~1;
     static constexpr int kRowBuf = RG * RP::BUF;
-    static constexpr int kColBuf = N1 * CW;
+    static constexpr int kColBuf = N1 * CS;
     static constexpr std::size_t kSmem = sizeof(float2) * (kTwR + kHalf + kTwC + kRowBuf + kColBuf);
 
     struct Smem {
@@ -118,11 +121,11 @@ __global__ void __launch_bounds__(T)
                 }
                 const int k = rt + i * RP::P;
                 if (act && k < m2) {
-                    s.colbuf[r * K::CW + k] = r2c_combine(v[i], zmk, s.half[k]);
+                    s.colbuf[r * K::CS + k] = r2c_combine(v[i], zmk, s.half[k]);
                 }
             }
             if (act && rt == 0 && M < m2) {  // the Nyquist output, X[M] = Z[0].x - Z[0].y
-                s.colbuf[r * K::CW + M] = r2c_combine(v[0], v[0], s.half[M]);
+                s.colbuf[r * K::CS + M] = r2c_combine(v[0], v[0], s.half[M]);
             }
         }
         __syncthreads();
@@ -130,10 +133,10 @@ __global__ void __launch_bounds__(T)
         float2 v[CP::E];
 #pragma unroll
         for (int i = 0; i < CP::E; ++i) {
-            v[i] = s.colbuf[(ct + i * CP::P) * K::CW + cc];
+            v[i] = s.colbuf[(ct + i * CP::P) * K::CS + cc];
         }
         __syncthreads();
-        run_passes<CP, false, B, K::CW, true>(v, ct, s.colbuf + cc, s.twc);
+        run_passes<CP, false, B, K::CS, true>(v, ct, s.colbuf + cc, s.twc);
         if (cc < m2) {
             float2* mf = modes + f * (2LL * m1 * m2);
 #pragma unroll
@@ -181,13 +184,13 @@ __global__ void __launch_bounds__(T)
             const int row = mode_row(ct + i * CP::P, N1, m1);
             v[i] = (cc < m2 && row >= 0) ? __ldg(mf + row * m2 + cc) : zero;
         }
-        run_passes<CP, true, B, K::CW, true>(v, ct, s.colbuf + cc, s.twc);
+        run_passes<CP, true, B, K::CS, true>(v, ct, s.colbuf + cc, s.twc);
         __syncthreads();  // the last exchange's reads (and the previous field's rows) are done
         constexpr float kColScale = 1.0f / N1;
         if (cc < m2) {
 #pragma unroll
             for (int i = 0; i < CP::E; ++i) {
-                s.colbuf[(ct + i * CP::P) * K::CW + cc] = cscale(v[i], kColScale);
+                s.colbuf[(ct + i * CP::P) * K::CS + cc] = cscale(v[i], kColScale);
             }
         }
         __syncthreads();
@@ -205,8 +208,8 @@ __global__ void __launch_bounds__(T)
                 const bool has_mk = act && M - k < m2;
                 u[i] = zero;
                 if (has_k || has_mk) {  // most of a row's spectrum is zero: skip it whole
-                    float2 xk = has_k ? s.colbuf[r * K::CW + k] : zero;
-                    float2 xmk = has_mk ? s.colbuf[r * K::CW + (M - k)] : zero;
+                    float2 xk = has_k ? s.colbuf[r * K::CS + k] : zero;
+                    float2 xmk = has_mk ? s.colbuf[r * K::CS + (M - k)] : zero;
                     if (k == 0) {
                         xk.y = 0.0f;
                         xmk.y = 0.0f;

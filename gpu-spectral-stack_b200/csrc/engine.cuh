@@ -20,10 +20,12 @@
 // writes output r to position (j - k) R + k + r L. The small radix (if log2 E does not divide
 // log2 N) goes first, where no twiddles are needed.
 //
-// Exchange layout: position p is stored at pad(p) = p + L * floor(p / (L R)) when L < 16, else
-// at p. For the strided writes of the early passes this puts the 16 threads of a half-warp on
-// 16 different 8-byte bank pairs; the reads of the next pass (consecutive positions) stay
-// conflict-free. The reference's stage store has 4.5 M bank conflicts per 2^24 points
+// Exchange layout: position p is stored at pad(p) = p + L * floor(p / W), W = max(L R, 16),
+// when L < 16, else at p. For the strided writes of the early passes this puts the 16 threads of
+// a half-warp on 16 different 8-byte bank pairs; the reads of the next pass (consecutive
+// positions) stay conflict-free because a group of 16 consecutive positions is never split by a
+// pad entry (with W = L R < 16, as for a radix-8 first pass, the reads of a half-warp would
+// straddle one and wrap onto a bank already in use). The reference's stage store has 4.5 M bank conflicts per 2^24 points
 // (docs/PROFILING.md:129-136); this layout has none for N >= 256.
 //
 // Twiddles live in shared memory, one table per pass after the first: entry r L + k of pass s
@@ -108,7 +110,7 @@ struct Plan {
     // Storage index of position p in the exchange that follows pass s.
     __host__ __device__ static constexpr int pad(int p, int s)
     {
-        return span(s) < 16 ? p + span(s) * (p / (span(s) * radix(s))) : p;
+        return span(s) < 16 ? p + span(s) * (p / cmax(span(s) * radix(s), 16)) : p;
     }
     // Slot length. The exchange accesses of one transform's P threads touch 2 P consecutive
     // banks (8-byte values); when P < 16, 32 / P transforms share a warp, and a slot length of
@@ -224,6 +226,7 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
     constexpr bool kLast = S == PL::PASSES - 1;
     constexpr int kTw = PL::tw_offset(S);
     constexpr bool kPad = Stride == 0 && L < 16;
+    constexpr int W = L * R < 16 ? 16 : L * R;  // positions per pad entry (a multiple of L R)
     static_assert(!Mirror || Q == 2, "mirror pairing needs two butterflies per thread");
     static_assert(Mirror || kLast || P % L == 0, "the plain exchange layout needs L to divide P");
 
@@ -264,7 +267,9 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
                 v[b + r * Q] = u[r];
             }
         } else {
-            const int base = (j - k) * (R + (kPad ? 1 : 0)) + k;
+            // The R outputs span L R consecutive positions inside one group of W.
+            const int pos0 = (j - k) * R + k;
+            const int base = kPad ? pos0 + L * (pos0 / W) : pos0;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 const int idx = base + r * L;
@@ -285,22 +290,22 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
 #pragma unroll
                 for (int r = 0; r < R2; ++r) {
                     const int q = j + r * NB2;
-                    const int idx = kPad ? q + L * (q / (L * R)) : q;
+                    const int idx = kPad ? q + L * (q / W) : q;
                     v[b + r * Q2] = buf[Stride == 0 ? idx : idx * Stride];
                 }
             }
-        } else if constexpr (kPad && P % (L * R) == 0) {
-            // pad(t + i P) = t + L floor(t / (L R)) + i (P + P / R), since L R divides P.
-            const int base = t + L * (t / (L * R));
+        } else if constexpr (kPad && P % W == 0) {
+            // pad(t + i P) = t + L floor(t / W) + i (P + L P / W), since W divides P.
+            const int base = t + L * (t / W);
 #pragma unroll
             for (int i = 0; i < E; ++i) {
-                v[i] = buf[base + i * (P + P / R)];
+                v[i] = buf[base + i * (P + L * P / W)];
             }
         } else if constexpr (kPad) {
 #pragma unroll
             for (int i = 0; i < E; ++i) {
                 const int q = t + i * P;
-                v[i] = buf[q + L * (q / (L * R))];
+                v[i] = buf[q + L * (q / W)];
             }
         } else {
 #pragma unroll

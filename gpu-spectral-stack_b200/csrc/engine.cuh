@@ -20,12 +20,14 @@
 // writes output r to position (j - k) R + k + r L. The small radix (if log2 E does not divide
 // log2 N) goes first, where no twiddles are needed.
 //
-// Exchange layout: position p is stored at pad(p) = p + L * floor(p / W), W = max(L R, 16),
-// when L < 16, else at p. For the strided writes of the early passes this puts the 16 threads of
-// a half-warp on 16 different 8-byte bank pairs; the reads of the next pass (consecutive
-// positions) stay conflict-free because a group of 16 consecutive positions is never split by a
-// pad entry (with W = L R < 16, as for a radix-8 first pass, the reads of a half-warp would
-// straddle one and wrap onto a bank already in use). The reference's stage store has 4.5 M bank conflicts per 2^24 points
+// Exchange layout: position p is stored at pad(p) = p + L * floor(p / W) when L < 16, else at
+// p; W = L R, or 16 where L R < 16 and a transform has at least 16 threads. For the strided
+// writes of the early passes this puts the 16 threads of a half-warp on 16 different 8-byte bank
+// pairs; the reads of the next pass (consecutive positions) stay conflict-free because, with
+// W >= 16, a half-warp's 16 consecutive positions are never split by a pad entry (with W = 8, as
+// for a radix-8 first pass, they would straddle one and wrap onto a bank already in use). Where
+// a transform has fewer than 16 threads, W = L R keeps each transform's writes spread so that
+// the transforms sharing a half-warp (slots P apart in banks) do not collide. The reference's stage store has 4.5 M bank conflicts per 2^24 points
 // (docs/PROFILING.md:129-136); this layout has none for N >= 256.
 //
 // Twiddles live in shared memory, one table per pass after the first: entry r L + k of pass s
@@ -108,9 +110,14 @@ struct Plan {
     static constexpr bool kPairLast = PASSES >= 1 && E / plan_radix(N, E, PASSES - 1, SmallLast) == 2;
 
     // Storage index of position p in the exchange that follows pass s.
+    // Positions per pad entry after pass s (see the exchange layout above).
+    __host__ __device__ static constexpr int pad_group(int s)
+    {
+        return (P >= 16 && span(s) * radix(s) < 16) ? 16 : span(s) * radix(s);
+    }
     __host__ __device__ static constexpr int pad(int p, int s)
     {
-        return span(s) < 16 ? p + span(s) * (p / cmax(span(s) * radix(s), 16)) : p;
+        return span(s) < 16 ? p + span(s) * (p / pad_group(s)) : p;
     }
     // Slot length. The exchange accesses of one transform's P threads touch 2 P consecutive
     // banks (8-byte values); when P < 16, 32 / P transforms share a warp, and a slot length of
@@ -226,7 +233,7 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
     constexpr bool kLast = S == PL::PASSES - 1;
     constexpr int kTw = PL::tw_offset(S);
     constexpr bool kPad = Stride == 0 && L < 16;
-    constexpr int W = L * R < 16 ? 16 : L * R;  // positions per pad entry (a multiple of L R)
+    constexpr int W = PL::pad_group(S);  // positions per pad entry (a multiple of L R)
     static_assert(!Mirror || Q == 2, "mirror pairing needs two butterflies per thread");
     static_assert(Mirror || kLast || P % L == 0, "the plain exchange layout needs L to divide P");
 

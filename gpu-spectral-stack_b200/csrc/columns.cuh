@@ -208,9 +208,14 @@ struct StridedIo {
 struct FourStepIo {
     const float2* x;
     float2* y;
-    int n2;       // columns of the first view (= the second pass's length)
+    int n2log;    // log2 of the columns of the first view (= the second pass's length)
     long long n;  // points per transform
     float scale;  // 1 / N1 for the inverse
+    // W_n^a = hi[a >> h] lo[a & (2^h - 1)]: two correctly rounded tables of 2^h and n / 2^h
+    // entries (L1-resident), one complex multiply instead of a sine and cosine per element.
+    const float2* tw_hi;
+    const float2* tw_lo;
+    int h;
 
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], const ColumnCtx& c) const
@@ -222,12 +227,14 @@ struct FourStepIo {
             }
             return;
         }
-        const long long b = c.f / n2;
-        const int col = static_cast<int>(c.f - b * n2);
-        const float2* base = x + b * n + col;
+        const long long b = c.f >> n2log;
+        const int col = static_cast<int>(c.f & ((1LL << n2log) - 1));
+        const float2* p = x + b * n + col + (static_cast<long long>(c.t) << n2log);
+        const long long step = static_cast<long long>(PL::P) << n2log;
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
-            v[i] = base[static_cast<long long>(c.t + i * PL::P) * n2];
+            v[i] = *p;
+            p += step;
         }
     }
 
@@ -235,18 +242,15 @@ struct FourStepIo {
     __device__ __forceinline__ void store(float2 (&v)[PL::E], const ColumnCtx& c) const
     {
         constexpr int N1 = PL::N;
-        const long long b = c.f / n2;
-        const int col = static_cast<int>(c.f - b * n2);
-        const float step = 2.0f / static_cast<float>(n);  // a power of two: exact
+        const int col = static_cast<int>(c.f & ((1LL << n2log) - 1));
+        const int lo_mask = (1 << h) - 1;
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
             const int k1 = c.t + i * PL::P;
-            // k1 col < n <= 2^24 is exact in float, so 2 k1 col / n is too.
-            float sn = 0.0f;
-            float cs = 1.0f;
-            sincospif(static_cast<float>(k1 * col) * step, &sn, &cs);
-            float2 w = cmul_tw<Inv>(v[i], make_float2(cs, -sn));
-            c.tile[c.c * (N1 + 1) + k1] = Inv ? cscale(w, scale) : w;
+            const int a = k1 * col;  // < n <= 2^24
+            const float2 w = cmul(__ldg(tw_hi + (a >> h)), __ldg(tw_lo + (a & lo_mask)));
+            const float2 r = cmul_tw<Inv>(v[i], w);
+            c.tile[c.c * (N1 + 1) + k1] = Inv ? cscale(r, scale) : r;
         }
         __syncthreads();
         for (int e = threadIdx.x; e < C * N1; e += C * PL::P) {
@@ -254,14 +258,27 @@ struct FourStepIo {
             const int k1 = e - cc * N1;
             const long long f = c.f0 + cc;
             if (f < c.transforms) {
-                const long long bb = f / n2;
-                const long long cl = f - bb * n2;
+                const long long bb = f >> n2log;
+                const long long cl = f & ((1LL << n2log) - 1);
                 y[bb * n + cl * N1 + k1] = c.tile[cc * (N1 + 1) + k1];
             }
         }
         __syncthreads();
     }
 };
+
+// The split-table twiddles W_n^a (a < n, n a power of two) of FourStepIo and the slab columns.
+struct TurnTables {
+    const float2* hi;
+    const float2* lo;
+    int h;
+};
+
+inline TurnTables turn_tables(long long n)
+{
+    const int h = (ilog2(static_cast<int>(n)) + 1) / 2;
+    return TurnTables{twiddles::turn(n >> h, static_cast<int>(n >> h)), twiddles::turn(n, 1 << h), h};
+}
 
 // Strided column plans with the CTAs per SM that the register budget must allow, from a sweep
 // on B200 (256-point columns of 256 fields x 129: 32.3 us at the compiler's own budget, two CTAs
@@ -300,10 +317,14 @@ struct ColumnEngine {
         dispatch_pow2<2, kMaxRowN>(n1, [&](auto n1_) {
             constexpr int N1 = decltype(n1_)::value;
             using PL = PlanFor<N1>;
+            const TurnTables tt = turn_tables(n);
+            const int n2log = ilog2(n2);
             if (d == Direction::Forward) {
-                launch_columns<PL, false, B, Table>(FourStepIo{x, y, n2, n, 1.0f}, batch * n2, s);
+                launch_columns<PL, false, B, Table>(FourStepIo{x, y, n2log, n, 1.0f, tt.hi, tt.lo, tt.h},
+                                                    batch * n2, s);
             } else {
-                launch_columns<PL, true, B, Table>(FourStepIo{x, y, n2, n, 1.0f / N1}, batch * n2, s);
+                launch_columns<PL, true, B, Table>(FourStepIo{x, y, n2log, n, 1.0f / N1, tt.hi, tt.lo, tt.h},
+                                                   batch * n2, s);
             }
         });
         columns(y, y, n2, n1, batch, 0, 0, d, s);

@@ -198,6 +198,11 @@ struct SlabColumnPass1Io {
     int n2;
     int n;
     float scale;  // 1 / n1 for the inverse
+    int wlog;     // log2 w
+    // W_n^a = hi[a >> h] lo[a & (2^h - 1)] (columns.cuh: TurnTables).
+    const float2* tw_hi;
+    const float2* tw_lo;
+    int h;
 
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], const ColumnCtx& c) const
@@ -223,17 +228,16 @@ struct SlabColumnPass1Io {
         if (!c.active) {
             return;
         }
-        const int q = static_cast<int>(c.f / w);
+        const int q = static_cast<int>(c.f >> wlog);
         float2* b = x + c.f;
         const long long stride = static_cast<long long>(n2) * w;
-        const float step = 2.0f / static_cast<float>(n);  // exact: n is a power of two
+        const int lo_mask = (1 << h) - 1;
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
             const int k1 = c.t + i * PL::P;
-            float sn = 0.0f;
-            float cs = 1.0f;
-            sincospif(static_cast<float>(k1 * q) * step, &sn, &cs);  // k1 q < n <= 2^14: exact
-            const float2 r = cmul_tw<Inv>(v[i], make_float2(cs, -sn));
+            const int a = k1 * q;  // < n
+            const float2 tw = cmul(__ldg(tw_hi + (a >> h)), __ldg(tw_lo + (a & lo_mask)));
+            const float2 r = cmul_tw<Inv>(v[i], tw);
             b[k1 * stride] = Inv ? cscale(r, scale) : r;
         }
     }
@@ -293,10 +297,11 @@ void slab_columns(float2* x, float2* y, int n, int w, cudaStream_t s)
     }
     const int n1 = 1 << (ilog2(n) / 2);
     const int n2 = n / n1;
+    const TurnTables tt = turn_tables(n);
     dispatch_pow2<2, kMaxRowN>(n1, [&](auto n1_) {
         constexpr int N1 = decltype(n1_)::value;
         launch_columns<PlanFor<N1>, Inv, 8, false>(
-            SlabColumnPass1Io{x, w, n2, n, Inv ? 1.0f / N1 : 1.0f},
+            SlabColumnPass1Io{x, w, n2, n, Inv ? 1.0f / N1 : 1.0f, ilog2(w), tt.hi, tt.lo, tt.h},
             static_cast<long long>(n2) * w, s);
     });
     dispatch_pow2<2, kMaxRowN>(n2, [&](auto n2_) {

@@ -211,11 +211,6 @@ struct FourStepIo {
     int n2log;    // log2 of the columns of the first view (= the second pass's length)
     long long n;  // points per transform
     float scale;  // 1 / N1 for the inverse
-    // W_n^a = hi[a >> h] lo[a & (2^h - 1)]: two correctly rounded tables of 2^h and n / 2^h
-    // entries (L1-resident), one complex multiply instead of a sine and cosine per element.
-    const float2* tw_hi;
-    const float2* tw_lo;
-    int h;
 
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], const ColumnCtx& c) const
@@ -243,13 +238,16 @@ struct FourStepIo {
     {
         constexpr int N1 = PL::N;
         const int col = static_cast<int>(c.f & ((1LL << n2log) - 1));
-        const int lo_mask = (1 << h) - 1;
+        const float step = 2.0f / static_cast<float>(n);  // a power of two: exact
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
             const int k1 = c.t + i * PL::P;
-            const int a = k1 * col;  // < n <= 2^24
-            const float2 w = cmul(__ldg(tw_hi + (a >> h)), __ldg(tw_lo + (a & lo_mask)));
-            const float2 r = cmul_tw<Inv>(v[i], w);
+            // k1 col < n <= 2^24 is exact in float, so 2 k1 col / n is too. (Two table loads and
+            // a complex multiply measured slower here than the arithmetic.)
+            float sn = 0.0f;
+            float cs = 1.0f;
+            sincospif(static_cast<float>(k1 * col) * step, &sn, &cs);
+            const float2 r = cmul_tw<Inv>(v[i], make_float2(cs, -sn));
             c.tile[c.c * (N1 + 1) + k1] = Inv ? cscale(r, scale) : r;
         }
         __syncthreads();
@@ -266,19 +264,6 @@ struct FourStepIo {
         __syncthreads();
     }
 };
-
-// The split-table twiddles W_n^a (a < n, n a power of two) of FourStepIo and the slab columns.
-struct TurnTables {
-    const float2* hi;
-    const float2* lo;
-    int h;
-};
-
-inline TurnTables turn_tables(long long n)
-{
-    const int h = (ilog2(static_cast<int>(n)) + 1) / 2;
-    return TurnTables{twiddles::turn(n >> h, static_cast<int>(n >> h)), twiddles::turn(n, 1 << h), h};
-}
 
 // Strided column plans with the CTAs per SM that the register budget must allow, from a sweep
 // on B200 (256-point columns of 256 fields x 129: 32.3 us at the compiler's own budget, two CTAs
@@ -317,14 +302,11 @@ struct ColumnEngine {
         dispatch_pow2<2, kMaxRowN>(n1, [&](auto n1_) {
             constexpr int N1 = decltype(n1_)::value;
             using PL = PlanFor<N1>;
-            const TurnTables tt = turn_tables(n);
             const int n2log = ilog2(n2);
             if (d == Direction::Forward) {
-                launch_columns<PL, false, B, Table>(FourStepIo{x, y, n2log, n, 1.0f, tt.hi, tt.lo, tt.h},
-                                                    batch * n2, s);
+                launch_columns<PL, false, B, Table>(FourStepIo{x, y, n2log, n, 1.0f}, batch * n2, s);
             } else {
-                launch_columns<PL, true, B, Table>(FourStepIo{x, y, n2log, n, 1.0f / N1, tt.hi, tt.lo, tt.h},
-                                                   batch * n2, s);
+                launch_columns<PL, true, B, Table>(FourStepIo{x, y, n2log, n, 1.0f / N1}, batch * n2, s);
             }
         });
         columns(y, y, n2, n1, batch, 0, 0, d, s);

@@ -199,10 +199,6 @@ struct SlabColumnPass1Io {
     int n;
     float scale;  // 1 / n1 for the inverse
     int wlog;     // log2 w
-    // W_n^a = hi[a >> h] lo[a & (2^h - 1)] (columns.cuh: TurnTables).
-    const float2* tw_hi;
-    const float2* tw_lo;
-    int h;
 
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], const ColumnCtx& c) const
@@ -231,13 +227,14 @@ struct SlabColumnPass1Io {
         const int q = static_cast<int>(c.f >> wlog);
         float2* b = x + c.f;
         const long long stride = static_cast<long long>(n2) * w;
-        const int lo_mask = (1 << h) - 1;
+        const float step = 2.0f / static_cast<float>(n);  // exact: n is a power of two
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
             const int k1 = c.t + i * PL::P;
-            const int a = k1 * q;  // < n
-            const float2 tw = cmul(__ldg(tw_hi + (a >> h)), __ldg(tw_lo + (a & lo_mask)));
-            const float2 r = cmul_tw<Inv>(v[i], tw);
+            float sn = 0.0f;
+            float cs = 1.0f;
+            sincospif(static_cast<float>(k1 * q) * step, &sn, &cs);  // k1 q < n <= 2^14: exact
+            const float2 r = cmul_tw<Inv>(v[i], make_float2(cs, -sn));
             b[k1 * stride] = Inv ? cscale(r, scale) : r;
         }
     }
@@ -297,11 +294,10 @@ void slab_columns(float2* x, float2* y, int n, int w, cudaStream_t s)
     }
     const int n1 = 1 << (ilog2(n) / 2);
     const int n2 = n / n1;
-    const TurnTables tt = turn_tables(n);
     dispatch_pow2<2, kMaxRowN>(n1, [&](auto n1_) {
         constexpr int N1 = decltype(n1_)::value;
         launch_columns<PlanFor<N1>, Inv, 8, false>(
-            SlabColumnPass1Io{x, w, n2, n, Inv ? 1.0f / N1 : 1.0f, ilog2(w), tt.hi, tt.lo, tt.h},
+            SlabColumnPass1Io{x, w, n2, n, Inv ? 1.0f / N1 : 1.0f, ilog2(w)},
             static_cast<long long>(n2) * w, s);
     });
     dispatch_pow2<2, kMaxRowN>(n2, [&](auto n2_) {

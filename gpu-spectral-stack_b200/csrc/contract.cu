@@ -183,21 +183,13 @@ __global__ void __launch_bounds__(256, 2)
             for (int oo = 0; oo < kOutPerThread; ++oo) {
                 wv[oo] = ws[(ic * kStagedOut + ob + oo) * kStagedModes + lane];
             }
-            // Each complex multiply-add as two FP32x2 FMAs on broadcast operands, in the order
-            // of the direct kernel's scalar FMAs (imaginary-part products first), so the two
-            // kernels round alike.
-            float2 wr[kOutPerThread];
-#pragma unroll
-            for (int oo = 0; oo < kOutPerThread; ++oo) {
-                wr[oo] = make_float2(-wv[oo].y, wv[oo].x);
-            }
 #pragma unroll
             for (int bb = 0; bb < kBatchPerThread; ++bb) {
-                const float2 xr = make_float2(xv[bb].x, xv[bb].x);
-                const float2 xi = make_float2(xv[bb].y, xv[bb].y);
 #pragma unroll
                 for (int oo = 0; oo < kOutPerThread; ++oo) {
-                    acc[bb][oo] = __ffma2_rn(xr, wv[oo], __ffma2_rn(xi, wr[oo], acc[bb][oo]));
+                    float2& a = acc[bb][oo];
+                    a.x = fmaf(xv[bb].x, wv[oo].x, fmaf(-xv[bb].y, wv[oo].y, a.x));
+                    a.y = fmaf(xv[bb].x, wv[oo].y, fmaf(xv[bb].y, wv[oo].x, a.y));
                 }
             }
         }

@@ -685,17 +685,31 @@ def run_ours(args) -> None:
         h2d, d2h = wl.io_bytes()
         hosts = [torch.from_numpy(wl.host_input(7000 + i)).pin_memory() for i in range(2)]
         outs = [torch.empty_like(h).pin_memory() for h in hosts]
-        for k in range(2):
-            outs[k % 2].copy_(wl.api_step(spectral, hosts[k % 2].cuda(non_blocking=True)), non_blocking=True)
+        # Two streams, steps alternating between them, as a user pipelines a stream of batches:
+        # step k + 1's host -> device copy runs beside step k's transforms and device -> host copy
+        # (PCIe is full duplex). Every step still copies its input in and its result out.
+        lanes = [torch.cuda.Stream(), torch.cuda.Stream()]
+
+        def e2e_step(k: int) -> None:
+            with torch.cuda.stream(lanes[k % 2]):
+                result = wl.api_step(spectral, hosts[k % 2].cuda(non_blocking=True))
+                outs[k % 2].copy_(result, non_blocking=True)
+
+        for k in range(4):
+            e2e_step(k)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e_start = torch.cuda.Event(enable_timing=True)
         e_stop = torch.cuda.Event(enable_timing=True)
-        e_steps = max(3, min(args.steps, 10))
+        e_steps = max(3, min(args.steps, 20))
         e_start.record(stream)
+        for lane in lanes:
+            lane.wait_event(e_start)
         for k in range(e_steps):
-            outs[k % 2].copy_(wl.api_step(spectral, hosts[k % 2].cuda(non_blocking=True)), non_blocking=True)
+            e2e_step(k)
+        for lane in lanes:
+            stream.wait_stream(lane)
         e_stop.record(stream)
         torch.cuda.synchronize()
         et = torch.tensor([e_start.elapsed_time(e_stop)], dtype=torch.float64, device="cuda")
@@ -703,7 +717,8 @@ def run_ours(args) -> None:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
         e2e = {"value": round(world * bytes_per_step * e_steps / (float(et.item()) * 1e-3) / 1e9, 3),
                "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "steps": e_steps, "path": "spectral.* torch ops -> C ABI, pinned host buffers"}
+               "steps": e_steps, "path": "spectral.* torch ops -> C ABI, pinned host buffers",
+               "pipeline": "2 streams, steps alternating: copies of neighbouring steps overlap"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

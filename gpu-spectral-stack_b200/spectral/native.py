@@ -61,6 +61,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_slab_rows": (_i, [_p, _p, _i, _ll, _i, _i, _p]),
     "spectral_slab_columns": (_i, [_p, _p, _i, _i, _i, _p]),
     "spectral_slab_rows_peer": (_i, [_p, _p, ctypes.POINTER(_p), _i, _ll, _i, _i, _i, _p]),
+    "spectral_fft2_slab_workspace": (_i, [_i, _i, _szp]),
+    "spectral_fft2_slab": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),
+    "spectral_slab_exchange": (_i, [_p, _p, _ll, _i, _p, _p]),
+    "spectral_nccl_unique_id": (_i, [_p]),
+    "spectral_nccl_comm_init": (_i, [_p, _i, _i, ctypes.POINTER(_p)]),
+    "spectral_nccl_comm_destroy": (_i, [_p]),
     "spectral_ipc_alloc": (_i, [ctypes.c_ulonglong, ctypes.POINTER(_p), _p]),
     "spectral_ipc_open": (_i, [_p, ctypes.POINTER(_p)]),
     "spectral_ipc_close": (_i, [_p]),

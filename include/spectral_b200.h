@@ -184,6 +184,26 @@ SPECTRAL_API int spectral_slab_rows_peer(const void* x, void* y, void* const* pe
                                          long long rows, int rank, int ranks, int inverse,
                                          void* stream);
 
+/* The whole slab transform through the C ABI, with the exchange on an NCCL communicator given as
+ * void* (ncclComm_t; no counterpart in the reference). Forward: x is this rank's n/ranks rows
+ * (rows x n), y receives its n x n/ranks column slab of fft2. Inverse: x is the column slab, y
+ * receives the rank's rows of ifft2 (divided by n^2). work: spectral_fft2_slab_workspace
+ * complex values. The library does not link NCCL: the entry points are resolved at run time
+ * from the libnccl.so.2 already loaded into the process (else the one the loader finds), so a
+ * communicator the caller made with its own NCCL works. spectral_slab_exchange is the exchange
+ * alone (chunk s of send to rank s, chunk s of recv from rank s, values_per_rank complex values
+ * each); spectral_nccl_* make and free a communicator for callers without NCCL of their own
+ * (the SPECTRAL_NCCL_ID_BYTES-byte id from one rank, passed to every rank). */
+#define SPECTRAL_NCCL_ID_BYTES 128
+SPECTRAL_API int spectral_fft2_slab_workspace(int n, int ranks, size_t* count);
+SPECTRAL_API int spectral_fft2_slab(const void* x, void* y, void* work, int n, int rank, int ranks,
+                                    int inverse, void* comm, void* stream);
+SPECTRAL_API int spectral_slab_exchange(const void* send, void* recv, long long values_per_rank, int ranks,
+                                        void* comm, void* stream);
+SPECTRAL_API int spectral_nccl_unique_id(void* id);
+SPECTRAL_API int spectral_nccl_comm_init(const void* id, int rank, int ranks, void** comm);
+SPECTRAL_API int spectral_nccl_comm_destroy(void* comm);
+
 /* Device buffers shared between the processes of one node through CUDA IPC, for the buffers
  * spectral_slab_rows_peer addresses: allocate (cudaMalloc on the current device) and export a
  * SPECTRAL_IPC_HANDLE_BYTES-byte handle; map another process's handle (peer access enabled on

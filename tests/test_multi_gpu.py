@@ -55,6 +55,34 @@ def _rank_main(rank: int, world: int, port: int, n: int) -> None:
             pback = plan.inverse(pcols)
             assert torch.equal(pback, back)
         plan.close()
+
+        # The same through the C ABI on an NCCL communicator of the library's own making.
+        import ctypes
+
+        from spectral import native
+
+        lib = native.lib()
+        uid = ctypes.create_string_buffer(128)
+        if rank == 0:
+            native.check(lib.spectral_nccl_unique_id(uid))
+        shared = [uid.raw]
+        dist.broadcast_object_list(shared, src=0)
+        comm = ctypes.c_void_p()
+        native.check(lib.spectral_nccl_comm_init(shared[0], rank, world, ctypes.byref(comm)))
+        count = ctypes.c_size_t(0)
+        native.check(lib.spectral_fft2_slab_workspace(n, world, ctypes.byref(count)))
+        work = torch.empty(count.value, dtype=torch.complex64, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        ccols = torch.empty_like(cols)
+        native.check(lib.spectral_fft2_slab(local.data_ptr(), ccols.data_ptr(), work.data_ptr(), n, rank,
+                                            world, 0, comm, stream))
+        cback = torch.empty_like(back)
+        native.check(lib.spectral_fft2_slab(ccols.data_ptr(), cback.data_ptr(), work.data_ptr(), n, rank,
+                                            world, 1, comm, stream))
+        torch.cuda.synchronize()
+        assert torch.equal(ccols, cols)
+        assert torch.equal(cback, back)
+        native.check(lib.spectral_nccl_comm_destroy(comm))
         dist.barrier()
     finally:
         dist.destroy_process_group()

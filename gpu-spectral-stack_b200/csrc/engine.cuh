@@ -657,9 +657,69 @@ struct C2cIo {
         }
     }
 
+    // One thread per transform (P = 1, N <= 16): each warp's 32 transforms are 32 N contiguous
+    // values, loaded and stored coalesced and transposed through the warp's own slots (odd
+    // length: both the [slot][position] writes and reads are conflict-free). Every lane takes
+    // part, active or not.
+    template <class PL>
+    __device__ __forceinline__ void load_warp_transposed(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        constexpr int N = PL::N;
+        const int lane = c.g & 31;
+        const int g0 = c.g - lane;
+        const int live = c.count - g0;  // transforms of this warp that exist (may be <= 0 or > 32)
+        const float2* src = x + (c.tf0 + g0) * N;
+        float2* slots = c.bufs + g0 * PL::BUF;
+        __syncwarp();  // every lane is done with its slot from the previous tile (the Io's store)
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const int e = i * 32 + lane;
+            const int g = e / N;
+            if (g < live) {
+                slots[g * PL::BUF + (e - g * N)] = __ldg(src + e);
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            v[i] = c.active ? slots[lane * PL::BUF + i] : make_float2(0.0f, 0.0f);
+        }
+    }
+
+    template <class PL, bool Inv>
+    __device__ __forceinline__ void store_warp_transposed(float2 (&v)[PL::E], const RowCtx& c) const
+    {
+        constexpr int N = PL::N;
+        const int lane = c.g & 31;
+        const int g0 = c.g - lane;
+        const int live = c.count - g0;
+        float2* dst = y + (c.tf0 + g0) * N;
+        float2* slots = c.bufs + g0 * PL::BUF;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            slots[lane * PL::BUF + i] = Inv ? cscale(v[i], scale) : v[i];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const int e = i * 32 + lane;
+            const int g = e / N;
+            if (g < live) {
+                dst[e] = slots[g * PL::BUF + (e - g * N)];
+            }
+        }
+        __syncwarp();  // the slots are read before the next tile's load refills them
+    }
+
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], const RowCtx& c) const
     {
+        if constexpr (PL::P == 1 && PL::N > 1) {
+            if (keep_in == PL::N) {
+                load_warp_transposed<PL>(v, c);
+                return;
+            }
+        }
         if (!c.active) {
 #pragma unroll
             for (int i = 0; i < PL::E; ++i) {
@@ -686,6 +746,12 @@ struct C2cIo {
     template <class PL, bool Inv>
     __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
     {
+        if constexpr (PL::P == 1 && PL::N > 1) {
+            if (keep_out == PL::N) {
+                store_warp_transposed<PL, Inv>(v, c);
+                return;
+            }
+        }
         if (!c.active) {
             return;
         }

@@ -65,8 +65,7 @@ struct RowChoice {
 __host__ __device__ constexpr RowChoice row_choice(RowKind k, int n)
 {
     if (k == RowKind::C2c) {
-        return n <= 8    ? RowChoice{kMinThreads, 1, true, false, false}
-             : n <= 64   ? RowChoice{kMinThreads, 1, true, false, true}
+        return n <= 64   ? RowChoice{kMinThreads, 1, true, false, true}
              : n == 128  ? RowChoice{128, 4, false, false, true}
              : n <= 1024 ? RowChoice{128, 4, false, false, false}
              : n == 2048 ? RowChoice{kMinThreads, 1, false, true, true}

@@ -27,14 +27,16 @@
 // W >= 16, a half-warp's 16 consecutive positions are never split by a pad entry (with W = 8, as
 // for a radix-8 first pass, they would straddle one and wrap onto a bank already in use). Where
 // a transform has fewer than 16 threads, W = L R keeps each transform's writes spread so that
-// the transforms sharing a half-warp (slots P apart in banks) do not collide. The reference's stage store has 4.5 M bank conflicts per 2^24 points
-// (docs/PROFILING.md:129-136); this layout has none for N >= 256.
+// the transforms sharing a half-warp (slots P apart in banks) do not collide. The reference's
+// stage store has 4.5 M bank conflicts per 2^24 points (docs/PROFILING.md:129-136).
 //
-// Twiddles live in shared memory, one table per pass after the first: entry r L + k of pass s
-// holds W_{L R}^(k r) = exp(-2 pi i k r / (L R)). Consecutive threads read consecutive entries,
-// so the reads are conflict-free. The tables are filled once per (persistent) CTA, either
-// computed on chip with sincospif (the "computed" variants) or copied from a correctly rounded
-// table built in double precision on the host (the "_table" variant, twiddles.cu).
+// Twiddles: one table per pass after the first, in shared memory or read from global memory
+// (rows.cuh chooses per size): entry r L + k of pass s holds W_{L R}^(k r) = exp(-2 pi i k r /
+// (L R)). Consecutive threads read consecutive entries, so the reads are conflict-free. A
+// shared-memory table is filled once per (persistent) CTA, computed on chip with sincospif (the
+// "computed" variants) or copied from a correctly rounded table built in double precision on the
+// host (the "_table" variant, twiddles.cu); a global-memory table is one of those two, built once
+// per device.
 
 #include "common.cuh"
 #include "dft.cuh"
@@ -838,24 +840,6 @@ struct R2cIo {
         C2cIo{x, nullptr, PL::N, PL::N, 1.0f}.template load<PL>(v, c);
     }
 
-    // Staged: a tile is count rows of N packed complex values, contiguous.
-    template <class PL>
-    __host__ __device__ static constexpr int staged_input_entries() { return PL::G * PL::N; }
-    template <class PL>
-    __device__ __forceinline__ void stage_src(long long tf0, int count, const float2*& src,
-                                              unsigned& bytes, int& shift) const
-    {
-        src = x + tf0 * PL::N;
-        bytes = static_cast<unsigned>(count) * static_cast<unsigned>(PL::N) * 8u;
-        shift = 0;
-    }
-    template <class PL>
-    __device__ __forceinline__ void load_staged(float2 (&v)[PL::E], const RowCtx& c,
-                                                const float2* tile) const
-    {
-        C2cIo{x, nullptr, PL::N, PL::N, 1.0f}.template load_staged<PL>(v, c, tile);
-    }
-
     template <class PL, bool Inv>
     __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
     {
@@ -898,42 +882,6 @@ struct C2rIo {
     __host__ __device__ static constexpr int extra() { return PL::N + 1; }
     template <class PL, bool Table>
     __device__ static void prologue(float2* w, const float2* table) { fill_half_turn<PL, Table>(w, table); }
-
-    // Staged: a tile is count rows of `keep` values, contiguous but (keep being odd) starting on an
-    // 8-byte boundary for odd first rows; the copy starts one value early then (shift = 1) and is
-    // rounded up to 16 bytes. The host uses this path only when batch * keep is even, so the
-    // rounded copy never reads past the end of x.
-    template <class PL>
-    __host__ __device__ static constexpr int staged_input_entries() { return PL::G * (PL::N + 1) + 2; }
-    template <class PL>
-    __device__ __forceinline__ void stage_src(long long tf0, int count, const float2*& src,
-                                              unsigned& bytes, int& shift) const
-    {
-        const float2* start = x + tf0 * keep;
-        shift = static_cast<int>((reinterpret_cast<unsigned long long>(start) >> 3) & 1u);
-        src = start - shift;
-        const unsigned values = static_cast<unsigned>(count) * static_cast<unsigned>(keep) + shift;
-        bytes = ((values + 1u) & ~1u) * 8u;
-    }
-    template <class PL>
-    __device__ __forceinline__ void load_staged(float2 (&v)[PL::E], const RowCtx& c,
-                                                const float2* tile) const
-    {
-        constexpr int N = PL::N;
-        const float2 zero = make_float2(0.0f, 0.0f);
-        const float2* row = tile + c.g * keep;
-#pragma unroll
-        for (int i = 0; i < PL::E; ++i) {
-            const int k = c.t + i * PL::P;
-            float2 xk = k < keep ? row[k] : zero;
-            float2 xmk = N - k < keep ? row[N - k] : zero;
-            if (k == 0) {
-                xk.y = 0.0f;
-                xmk.y = 0.0f;
-            }
-            v[i] = c.active ? c2r_prepare(xk, xmk, c.extra[k]) : zero;
-        }
-    }
 
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], const RowCtx& c) const
@@ -1040,23 +988,6 @@ struct R2cPairIo {
     {
         C2cIo{x, nullptr, PL::N, PL::N, 1.0f}.template load<PL>(v, c);
     }
-    template <class PL>
-    __host__ __device__ static constexpr int staged_input_entries() { return PL::G * PL::N; }
-    template <class PL>
-    __device__ __forceinline__ void stage_src(long long tf0, int count, const float2*& src,
-                                              unsigned& bytes, int& shift) const
-    {
-        src = x + tf0 * PL::N;
-        bytes = static_cast<unsigned>(count) * static_cast<unsigned>(PL::N) * 8u;
-        shift = 0;
-    }
-    template <class PL>
-    __device__ __forceinline__ void load_staged(float2 (&v)[PL::E], const RowCtx& c,
-                                                const float2* tile) const
-    {
-        C2cIo{x, nullptr, PL::N, PL::N, 1.0f}.template load_staged<PL>(v, c, tile);
-    }
-
     template <class PL, bool Inv>
     __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
     {
@@ -1208,31 +1139,6 @@ struct C2rPairIo {
         const float2* row = x + c.tf * keep;
         const int kp = keep;
         prepare<PL>(v, c, [&](int k) { return k < kp ? __ldg(row + k) : zero; });
-    }
-
-    template <class PL>
-    __host__ __device__ static constexpr int staged_input_entries() { return PL::G * (PL::N + 1) + 2; }
-    template <class PL>
-    __device__ __forceinline__ void stage_src(long long tf0, int count, const float2*& src,
-                                              unsigned& bytes, int& shift) const
-    {
-        C2rIo{x, y, keep, scale}.template stage_src<PL>(tf0, count, src, bytes, shift);
-    }
-    template <class PL>
-    __device__ __forceinline__ void load_staged(float2 (&v)[PL::E], const RowCtx& c,
-                                                const float2* tile) const
-    {
-        const float2 zero = make_float2(0.0f, 0.0f);
-        if (!c.active) {
-#pragma unroll
-            for (int i = 0; i < PL::E; ++i) {
-                v[i] = zero;
-            }
-            return;
-        }
-        const float2* row = tile + c.g * keep;
-        const int kp = keep;
-        prepare<PL>(v, c, [&](int k) { return k < kp ? row[k] : zero; });
     }
 
     template <class PL, bool Inv>

@@ -90,7 +90,7 @@ void launch_columns(const Io& io, long long transforms, cudaStream_t stream)
     auto kernel = column_kernel<PL, C, Inv, B, Table, Io>;
     constexpr std::size_t smem = column_smem_bytes<PL, C>();
     static std::atomic<int> cache[kMaxDevices];
-    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::RE) : nullptr;
+    const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E) : nullptr;
     const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), C * PL::P, smem,
                                           cache, (transforms + C - 1) / C);
     launch_pdl(kernel, grid, static_cast<unsigned>(C * PL::P), smem, stream, io, transforms, tw);

@@ -91,31 +91,25 @@ __host__ __device__ constexpr int plan_tw_entries(int n, int e, bool small_last 
     return plan_tw_offset(n, e, plan_passes(n, e), small_last);
 }
 
-// RMax caps the radix of a pass below the points per thread (RE = min(E, RMax)): the pass
-// structure, and so the twiddle tables, are those of an (N, RE) plan, while each thread holds E
-// points as E / R butterflies per pass.
-template <int N_, int E_, bool SmallLast_ = false, int MinThreads_ = kMinThreads, int MinBlocks_ = 1,
-          int RMax_ = 32>
+template <int N_, int E_, bool SmallLast_ = false, int MinThreads_ = kMinThreads, int MinBlocks_ = 1>
 struct Plan {
     static constexpr int N = N_;
     static constexpr int MIN_BLOCKS = MinBlocks_;  // CTAs per SM the register budget must allow
     static constexpr int E = E_;
-    static constexpr int RE = E_ < RMax_ ? E_ : RMax_;  // the radix structure's E
     static constexpr bool SmallLast = SmallLast_;
     static_assert(is_pow2(N) && is_pow2(E) && E <= N && E <= 32 && (N == 1 || E >= 2), "bad plan");
-    static_assert(is_pow2(RE) && (N == 1 || RE >= 2), "bad radix cap");
     static constexpr int P = N / E;  // threads per transform
-    static constexpr int PASSES = plan_passes(N, RE);
+    static constexpr int PASSES = plan_passes(N, E);
     static constexpr int THREADS = cmax(MinThreads_, P);  // a CTA holds G = THREADS / P transforms
     static constexpr int G = THREADS / P;  // transforms per CTA
 
-    __host__ __device__ static constexpr int radix(int s) { return plan_radix(N, RE, s, SmallLast); }
-    __host__ __device__ static constexpr int span(int s) { return plan_span(N, RE, s, SmallLast); }
-    __host__ __device__ static constexpr int tw_offset(int s) { return plan_tw_offset(N, RE, s, SmallLast); }
-    static constexpr int TW = plan_tw_entries(N, RE, SmallLast);  // entries of all the pass tables
+    __host__ __device__ static constexpr int radix(int s) { return plan_radix(N, E, s, SmallLast); }
+    __host__ __device__ static constexpr int span(int s) { return plan_span(N, E, s, SmallLast); }
+    __host__ __device__ static constexpr int tw_offset(int s) { return plan_tw_offset(N, E, s, SmallLast); }
+    static constexpr int TW = plan_tw_entries(N, E, SmallLast);  // entries of all the pass tables
     // Two butterflies per thread in the first / last pass: mirror pairing is possible there.
-    static constexpr bool kPairFirst = PASSES >= 1 && E / plan_radix(N, RE, 0, SmallLast) == 2;
-    static constexpr bool kPairLast = PASSES >= 1 && E / plan_radix(N, RE, PASSES - 1, SmallLast) == 2;
+    static constexpr bool kPairFirst = PASSES >= 1 && E / plan_radix(N, E, 0, SmallLast) == 2;
+    static constexpr bool kPairLast = PASSES >= 1 && E / plan_radix(N, E, PASSES - 1, SmallLast) == 2;
 
     // Storage index of position p in the exchange that follows pass s.
     // Positions per pad entry after pass s (see the exchange layout above).

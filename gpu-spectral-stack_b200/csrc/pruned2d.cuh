@@ -254,9 +254,9 @@ struct Pruned2dEngine {
         using K = Pruned2d<N1, N2, B, Table, T>;
         auto kernel = Forward ? pruned2d_forward<N1, N2, B, Table, T> : pruned2d_inverse<N1, N2, B, Table, T>;
         static std::atomic<int> cache[kMaxDevices];
-        const float2* twr = Table ? twiddles::pass_table(K::M, K::RP::RE) : nullptr;
+        const float2* twr = Table ? twiddles::pass_table(K::M, K::RP::E) : nullptr;
         const float2* half = Table ? twiddles::half_turn(K::M) : nullptr;
-        const float2* twc = Table ? twiddles::pass_table(N1, K::CP::RE) : nullptr;
+        const float2* twc = Table ? twiddles::pass_table(N1, K::CP::E) : nullptr;
         const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), K::THREADS,
                                               K::kSmem, cache, fields);
         launch_pdl(kernel, grid, static_cast<unsigned>(K::THREADS), K::kSmem, stream, in, out, fields,

@@ -105,11 +105,11 @@ template <class PL, bool Table, bool SmemTw>
 const float2* row_pass_table()
 {
     if constexpr (Table) {
-        return twiddles::pass_table(PL::N, PL::RE, PL::SmallLast);
+        return twiddles::pass_table(PL::N, PL::E, PL::SmallLast);
     } else if constexpr (SmemTw) {
         return nullptr;
     } else {
-        return twiddles::pass_table_computed(PL::N, PL::RE, PL::SmallLast);
+        return twiddles::pass_table_computed(PL::N, PL::E, PL::SmallLast);
     }
 }
 

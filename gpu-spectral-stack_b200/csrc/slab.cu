@@ -182,7 +182,7 @@ void slab_rows(int n, long long rows, cudaStream_t s, MakeIo&& make_io)
         auto kernel = slab_row_kernel<PL, Inv, std::decay_t<decltype(io)>>;
         constexpr std::size_t smem = sizeof(float2) * static_cast<std::size_t>(PL::G) * PL::BUF;
         static std::atomic<int> cache[kMaxDevices];
-        const float2* tw = twiddles::pass_table(PL::N, PL::RE);
+        const float2* tw = twiddles::pass_table(PL::N, PL::E);
         const unsigned grid = persistent_grid(reinterpret_cast<const void*>(kernel), PL::THREADS,
                                               smem, cache, (rows + PL::G - 1) / PL::G);
         launch_pdl(kernel, grid, static_cast<unsigned>(PL::THREADS), smem, s, io, tw);

@@ -726,8 +726,13 @@ def run_ours(args) -> None:
         rows = cpu_sample_rows(wl)
         cpu_time(wl, rows, threads, 1)
         t_cpu, nbytes = cpu_time(wl, rows, threads, 3)
+        # numpy's FFT is single-threaded: one core is the reference's CPU path as a user runs it.
+        rows1 = max(1, rows // max(1, threads))
+        t_one, bytes_one = cpu_time(wl, rows1, 1, 3)
         cpu = {"value": round(nbytes / t_cpu / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"oracle (numpy pocketfft float64) on {rows} rows of the workload, best of 3, {threads} threads"}
+               "sample": f"oracle (numpy pocketfft float64) on {rows} rows of the workload, best of 3, {threads} threads",
+               "one_core": {"value": round(bytes_one / t_one / 1e9, 3), "unit": UNIT,
+                            "sample": f"{rows1} rows, best of 3, 1 thread"}}
 
     faults = native.device_faults()
     if world > 1:

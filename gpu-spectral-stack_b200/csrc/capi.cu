@@ -171,6 +171,16 @@ std::size_t real_work(const Impl& impl, int n1, int n2, long long batch)
     return impl.real_needs_work ? count3(batch, n1, n2 / 2) : 0;
 }
 
+// Every array is read and written as 8-byte values (complex float2; real arrays two samples at
+// a time), so every pointer must be 8-byte aligned; a misaligned one is refused before any
+// launch.
+void need_aligned(const void* p, const char* who)
+{
+    if ((reinterpret_cast<unsigned long long>(p) & 7u) != 0) {
+        throw InvalidArgument(std::string(who) + ": arrays must be 8-byte aligned");
+    }
+}
+
 void need_work(const void* work, std::size_t count, const char* who)
 {
     need(count == 0 || work != nullptr, std::string(who) + ": this call needs a workspace of "
@@ -344,6 +354,8 @@ int run_fft2_c2r_strided(const char* impl, const void* x, float* y, int n1, int 
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "fft2_c2r");
+        need_aligned(y, "fft2_c2r");
         need(i.has_columns(), std::string(impl) + " has no strided column kernel");
         check_2d(i, Columns::Strided, n1, n2, batch, true);
         const std::size_t needed = fft2_c2r_work(i, Columns::Strided, n1, n2, batch);
@@ -407,6 +419,8 @@ int spectral_c2c(const char* impl, const void* x, void* y, int n, long long batc
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "fft");
+        need_aligned(y, "fft");
         check_c2c(i, x, y, n, batch, n, n, "fft");
         c2c_any(i, static_cast<const float2*>(x), static_cast<float2*>(y), n, batch,
                 inverse ? Direction::Inverse : Direction::Forward, n, as_stream(stream));
@@ -423,6 +437,8 @@ int spectral_r2c(const char* impl, const float* x, void* y, int n, long long bat
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "r2c");
+        need_aligned(y, "r2c");
         check_real(i, x, y, n, batch, n / 2 + 1, "r2c");
         need_work(work, real_work(i, 1, n, batch), "r2c");
         i.backend->r2c(x, static_cast<float2*>(y), n, batch, n / 2 + 1, static_cast<float2*>(work),
@@ -435,6 +451,8 @@ int spectral_c2r(const char* impl, const void* x, float* y, int n, long long bat
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "c2r");
+        need_aligned(y, "c2r");
         check_real(i, y, x, n, batch, n / 2 + 1, "c2r");
         need_work(work, real_work(i, 1, n, batch), "c2r");
         i.backend->c2r(static_cast<const float2*>(x), y, n, batch, n / 2 + 1,
@@ -447,6 +465,8 @@ int spectral_columns(const char* impl, const void* x, void* y, int n, int cols, 
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "columns");
+        need_aligned(y, "columns");
         need(i.has_columns(), std::string(i.name) + " has no strided column kernel");
         need(is_pow2(n) && n <= i.max_n, "columns: n must be a power of two from 1 to "
                                              + str(i.max_n) + ", got " + str(n));
@@ -479,6 +499,8 @@ int spectral_fft2_c2c(const char* impl, int columns, const void* x, void* y, int
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "fft2_c2c");
+        need_aligned(y, "fft2_c2c");
         const Columns c = to_columns(columns);
         check_2d(i, c, n1, n2, batch, false);
         need_work(work, fft2_c2c_work(i, c, n1, n2, batch), "fft2_c2c");
@@ -493,6 +515,8 @@ int spectral_fft2_r2c(const char* impl, int columns, const float* x, void* y, in
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "fft2_r2c");
+        need_aligned(y, "fft2_r2c");
         const Columns c = to_columns(columns);
         check_2d(i, c, n1, n2, batch, true);
         need_work(work, fft2_r2c_work(i, c, n1, n2, batch), "fft2_r2c");
@@ -506,6 +530,8 @@ int spectral_fft2_c2r(const char* impl, int columns, const void* x, float* y, in
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "fft2_c2r");
+        need_aligned(y, "fft2_c2r");
         const Columns c = to_columns(columns);
         check_2d(i, c, n1, n2, batch, true);
         need_work(work, fft2_c2r_work(i, c, n1, n2, batch), "fft2_c2r");
@@ -524,6 +550,8 @@ int spectral_c2c_pruned(const char* impl, const void* x, void* y, int n, int kee
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "fft_c2c_pruned");
+        need_aligned(y, "fft_c2c_pruned");
         check_pruned_1d(i, n, keep, batch);
         const Direction d = inverse ? Direction::Inverse : Direction::Forward;
         const auto* xs = static_cast<const float2*>(x);
@@ -566,6 +594,8 @@ int spectral_rfft2_modes(const char* impl, const float* x, void* modes, int n1, 
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(x, "rfft2_modes");
+        need_aligned(modes, "rfft2_modes");
         check_pruned_2d(i, n1, n2, m1, m2, batch);
         need_work(work, rfft2_modes_work(i, n1, n2, m1, m2, batch), "rfft2_modes");
         auto* ms = static_cast<float2*>(modes);
@@ -592,6 +622,8 @@ int spectral_irfft2_modes(const char* impl, const void* modes, float* y, int n1,
 {
     return guarded([&] {
         const Impl& i = find(impl);
+        need_aligned(modes, "irfft2_modes");
+        need_aligned(y, "irfft2_modes");
         check_pruned_2d(i, n1, n2, m1, m2, batch);
         need_work(work, irfft2_modes_work(i, n1, n2, m1, m2, batch), "irfft2_modes");
         const auto* ms = static_cast<const float2*>(modes);

@@ -224,6 +224,11 @@ extern "C" int spectral_mode_contract(const void* x, const void* w, void* out, l
         set_last_error("mode_contract: need batch >= 0, cin >= 1, cout >= 1, modes >= 0");
         return SPECTRAL_INVALID_ARGUMENT;
     }
+    if (((reinterpret_cast<unsigned long long>(x) | reinterpret_cast<unsigned long long>(w)
+          | reinterpret_cast<unsigned long long>(out)) & 7u) != 0) {
+        set_last_error("mode_contract: arrays must be 8-byte aligned");
+        return SPECTRAL_INVALID_ARGUMENT;
+    }
     if (batch == 0 || modes == 0) {
         return SPECTRAL_OK;
     }

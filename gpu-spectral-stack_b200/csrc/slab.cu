@@ -308,6 +308,13 @@ void slab_columns(float2* x, float2* y, int n, int w, cudaStream_t s)
     });
 }
 
+void check_aligned(const void* p)
+{
+    if ((reinterpret_cast<unsigned long long>(p) & 7u) != 0) {
+        throw InvalidArgument("fft2_slab: arrays must be 8-byte aligned");
+    }
+}
+
 void check_slab(int n, int ranks)
 {
     if (!is_pow2(n) || n < 2 || n > kMaxSlabN) {
@@ -344,6 +351,8 @@ extern "C" int spectral_slab_rows(const void* x, void* y, int n, long long rows,
     using namespace spectral;
     return slab_guarded([&] {
         check_slab(n, ranks);
+        check_aligned(x);
+        check_aligned(y);
         if (rows < 1 || rows > INT_MAX) {
             throw InvalidArgument("fft2_slab: rows must be from 1 to INT_MAX");
         }
@@ -380,6 +389,8 @@ extern "C" int spectral_slab_rows_peer(const void* x, void* y, void* const* peer
         if (peers == nullptr) {
             throw InvalidArgument("fft2_slab: peers must list one buffer per rank");
         }
+        check_aligned(x);
+        check_aligned(y);
         PeerSlabs ps = {};
         for (int q = 0; q < ranks; ++q) {
             if (peers[q] == nullptr) {
@@ -408,6 +419,8 @@ extern "C" int spectral_slab_columns(void* x, void* y, int n, int width, int inv
     using namespace spectral;
     return slab_guarded([&] {
         check_slab(n, 1);
+        check_aligned(x);
+        check_aligned(y);
         if (width < 1) {
             throw InvalidArgument("fft2_slab: width must be at least 1");
         }

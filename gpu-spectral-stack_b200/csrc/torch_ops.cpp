@@ -95,6 +95,17 @@ int batch_of(const at::Tensor& x, int64_t row, const char* op)
     return static_cast<int>(batch);
 }
 
+// The library reads and writes every array as 8-byte values; a contiguous float32 view can start
+// at an odd element, so such an input is copied to a fresh (aligned) allocation first.
+at::Tensor contiguous_aligned(const at::Tensor& x)
+{
+    at::Tensor c = x.contiguous();
+    if ((reinterpret_cast<uintptr_t>(c.const_data_ptr()) & 7u) != 0) {
+        c = c.clone(at::MemoryFormat::Contiguous);
+    }
+    return c;
+}
+
 at::Tensor workspace(size_t count, const at::Tensor& like)
 {
     return at::empty({static_cast<int64_t>(count)}, like.options().dtype(at::kComplexFloat));
@@ -112,7 +123,7 @@ at::Tensor scale_cuda(const at::Tensor& x, double alpha)
 {
     check_complex64_cuda(x, "x");
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
     at::Tensor y = at::empty_like(xc);
     check_status(spectral_scale(cptr(xc), mptr(y), static_cast<size_t>(xc.numel()),
                                 static_cast<float>(alpha), stream()));
@@ -133,7 +144,7 @@ at::Tensor fft_c2c_cuda(const at::Tensor& x, bool inverse, c10::string_view impl
                 impl.max_c2c_n, ", got ", n);
     const int batch = batch_of(x, n, "fft_c2c");
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
     at::Tensor y = at::empty_like(xc);
     check_status(spectral_c2c(impl.name.c_str(), cptr(xc), mptr(y), static_cast<int>(n), batch,
                               inverse ? 1 : 0, stream()));
@@ -155,7 +166,7 @@ at::Tensor fft_r2c_cuda(const at::Tensor& x, c10::string_view impl_name)
     }
     const int batch = batch_of(x, n, "fft_r2c");
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
     size_t count = 0;
     check_status(spectral_real_workspace(impl.name.c_str(), static_cast<int>(n), batch, &count));
     at::Tensor work = workspace(count, x);
@@ -180,7 +191,7 @@ at::Tensor fft_c2r_cuda(const at::Tensor& x, int64_t n, c10::string_view impl_na
     }
     const int batch = batch_of(x, n / 2 + 1, "fft_c2r");
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
     size_t count = 0;
     check_status(spectral_real_workspace(impl.name.c_str(), static_cast<int>(n), batch, &count));
     at::Tensor work = workspace(count, x);
@@ -232,7 +243,7 @@ at::Tensor fft2_c2c_cuda(const at::Tensor& x, bool inverse, c10::string_view imp
     }
     const Shape2d s = shape2d(x, x.size(-1), x.size(-1), "fft2_c2c");
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
     at::Tensor y = at::empty_like(xc);
     const auto n1 = static_cast<int>(s.n1);
     const auto n2 = static_cast<int>(s.n2);
@@ -260,7 +271,7 @@ at::Tensor fft2_r2c_cuda(const at::Tensor& x, c10::string_view impl_name, c10::s
     }
     const Shape2d s = shape2d(x, n2, n2, "fft2_r2c");
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
     const auto n1 = static_cast<int>(s.n1);
     size_t count = 0;
     check_status(spectral_fft2_r2c_workspace(impl.name.c_str(), method, n1, static_cast<int>(n2),
@@ -289,7 +300,7 @@ at::Tensor fft2_c2r_cuda(const at::Tensor& x, int64_t n2, c10::string_view impl_
     }
     const Shape2d s = shape2d(x, n2, n2 / 2 + 1, "fft2_c2r");
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
     const auto n1 = static_cast<int>(s.n1);
     size_t count = 0;
     check_status(spectral_fft2_c2r_workspace(impl.name.c_str(), method, n1, static_cast<int>(n2),
@@ -319,7 +330,7 @@ at::Tensor fft_c2c_pruned_cuda(const at::Tensor& x, int64_t n, int64_t keep, boo
     }
     const int batch = batch_of(x, row_in, "fft_c2c_pruned");
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
     size_t count = 0;
     check_status(spectral_c2c_pruned_workspace(impl.name.c_str(), static_cast<int>(n),
                                                static_cast<int>(keep), batch, &count));
@@ -349,7 +360,7 @@ at::Tensor rfft2_modes_cuda(const at::Tensor& x, int64_t m1, int64_t m2, c10::st
     }
     const int batch = batch_of(x, n1 * n2, "rfft2_modes");
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
     const int a = static_cast<int>(n1);
     const int b = static_cast<int>(n2);
     const int p = static_cast<int>(m1);
@@ -382,7 +393,7 @@ at::Tensor irfft2_modes_cuda(const at::Tensor& modes, int64_t n1, int64_t n2,
     }
     const int batch = batch_of(modes, two_m1 * m2, "irfft2_modes");
     const c10::cuda::CUDAGuard guard(modes.device());
-    const at::Tensor mc = modes.contiguous();
+    const at::Tensor mc = contiguous_aligned(modes);
     const int a = static_cast<int>(n1);
     const int b = static_cast<int>(n2);
     const int p = static_cast<int>(two_m1 / 2);
@@ -420,8 +431,8 @@ at::Tensor mode_contract_cuda(const at::Tensor& x, const at::Tensor& w)
         return y;
     }
     const c10::cuda::CUDAGuard guard(x.device());
-    const at::Tensor xc = x.contiguous();
-    const at::Tensor wc = w.contiguous();
+    const at::Tensor xc = contiguous_aligned(x);
+    const at::Tensor wc = contiguous_aligned(w);
     const int64_t modes = x.numel() / (x.size(0) * x.size(1));
     check_status(spectral_mode_contract(cptr(xc), cptr(wc), mptr(y), x.size(0),
                                         static_cast<int>(x.size(1)), static_cast<int>(w.size(1)),

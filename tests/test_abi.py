@@ -80,6 +80,25 @@ def test_argument_checks_use_the_reference_messages(fn, args, message):
         native.call(fn, *args)
 
 
+@pytest.mark.parametrize(
+    ("fn", "args"),
+    [
+        ("spectral_r2c", (b"stockham_r8", 4100, 8192, 64, 1, 0, None)),
+        ("spectral_c2r", (b"stockham_r8", 8192, 4100, 64, 1, 0, None)),
+        ("spectral_fft2_r2c", (b"stockham_r8", 1, 4100, 8192, 8, 8, 1, 0, None)),
+        ("spectral_rfft2_modes", (b"stockham_r8", 4100, 8192, 8, 8, 2, 2, 1, 0, None)),
+        ("spectral_c2c", (b"stockham_r8", 4100, 8192, 8, 1, 0, None)),
+        ("spectral_mode_contract", (4100, 8192, 16384, 1, 1, 1, 1, None)),
+        ("spectral_slab_rows", (4100, 8192, 8, 8, 1, 0, None)),
+    ],
+)
+def test_misaligned_arrays_are_refused_before_any_launch(fn, args):
+    # The kernels read every array as 8-byte values; a 4-byte-aligned float32 pointer (a view
+    # that starts at an odd element) is refused with a message instead of faulting the GPU.
+    with pytest.raises(ValueError, match="8-byte aligned"):
+        native.call(fn, *args)
+
+
 def test_workspace_sizes_follow_the_drivers():
     # Strided 2D needs none; the transpose method two arrays; the engine's real transforms none;
     # naive's real transforms batch * n/2 complex values.

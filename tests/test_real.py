@@ -141,3 +141,19 @@ def test_rejects_wrong_dtypes():
         spectral.rfft(torch.zeros(2, 8, dtype=torch.complex64, device="cuda"))
     with pytest.raises(RuntimeError, match="complex64"):
         spectral.irfft(torch.zeros(2, 5, device="cuda"), 8)
+
+
+def test_odd_offset_float_views_are_accepted(rng):
+    # A contiguous float32 view that starts at an odd element is 4-byte aligned; the operators
+    # copy it to an aligned allocation instead of handing it to the kernels.
+    flat = torch.from_numpy(random_real(rng, (3 * 256 + 1,))).cuda()
+    x = flat[1:].view(3, 256)
+    assert x.data_ptr() % 8 == 4
+    assert_transform_close(spectral.rfft(x, impl="stockham_r8"), ref.rfft(x.cpu().numpy()), 256)
+    flat2 = torch.from_numpy(random_real(rng, (2 * 32 * 32 + 1,))).cuda()
+    u = flat2[1:].view(2, 32, 32)
+    assert_transform_close(spectral.rfft2(u, impl="stockham_r8"), ref.rfft2(u.cpu().numpy()), 1024,
+                           axes=(-2, -1))
+    modes = spectral.rfft2_truncated(u, 4, 4, impl="stockham_r8")
+    assert modes.shape == (2, 8, 4)
+

@@ -1,7 +1,7 @@
 """Benchmark of the batched-FFT hot path: one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload real|c2c|rfft2|pruned] [--fft-impl stockham_r8]
+                    [--workload real|c2c|rfft2|pruned|slab|spectrum|fir] [--fft-impl stockham_r8]
 
 The headline workload is the one the metric is quoted on (configs[1] of BASELINE.json): a step
 is rfft then irfft of 4096 rows of 4096 float32 samples, iid U[-1, 1] from a seed, 2^24 points
@@ -59,7 +59,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=500)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["real", "c2c", "rfft2", "pruned", "slab"], default="real")
+    p.add_argument("--workload", choices=["real", "c2c", "rfft2", "pruned", "slab", "spectrum", "fir"],
+                   default="real")
     p.add_argument("--fft-impl", default="stockham_r8", help="registry name (spectral.FFT_IMPLS)")
     p.add_argument("--columns", default="strided", help="rfft2 workload: strided or transpose")
     p.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
@@ -308,6 +309,116 @@ class Pruned:
         return 2 * rows * self.channels * (4 * self.n * self.n + 16 * self.m * self.m)
 
 
+class Spectrum:
+    """The windowed spectrum (the reference's rf.spectrum): 16 complex64 signals of 2^20 N(0, 1)
+    samples (2^24 points), frames of 1024 with the Hann window; one fused kernel (framing and
+    window in the load). Bytes: 8 read + 8 written per sample."""
+
+    name = "rf.spectrum nfft=1024 hann, 16 x 2^20 c64 N(0,1)"
+
+    def __init__(self, impl: str, rows: int = 16, n: int = 1 << 20, nfft: int = 1024):
+        self.impl, self.rows, self.n, self.nfft = impl, rows, n, nfft
+        self.bytes_per_call = 16 * rows * n
+
+    def host_input(self, seed):
+        rng = np.random.default_rng(seed)
+        shape = (self.rows, self.n)
+        return ((rng.standard_normal(shape) + 1j * rng.standard_normal(shape)) / np.sqrt(2.0)).astype(np.complex64)
+
+    def device_sets(self, torch, seed):
+        from spectral import rf
+
+        self.window = rf.window("hann", self.nfft, device="cuda")
+        sets = []
+        for i in range(SETS):
+            x = torch.from_numpy(self.host_input(seed + i)).cuda()
+            sets.append((x, torch.empty(self.rows, self.n // self.nfft, self.nfft, dtype=torch.complex64, device="cuda")))
+        return sets
+
+    def kernels(self):
+        return [("spectrum", self.bytes_per_call)]
+
+    def launches_per_step(self) -> int:
+        return 1
+
+    def launch(self, native, sets, k, stream, which):
+        x, y = sets[k % SETS]
+        native.call("spectral_spectrum", self.impl.encode(), x.data_ptr(), self.window.data_ptr(), y.data_ptr(),
+                    self.n, self.nfft, self.rows, stream)
+
+    def api_step(self, spectral, x_dev):
+        from spectral import rf
+
+        return rf.spectrum(x_dev, self.nfft, window_name="hann", fft_impl=self.impl)
+
+    def io_bytes(self):
+        return 8 * self.rows * self.n, 8 * self.rows * self.n
+
+    def cpu_step(self, ref, x):
+        from oracle import rf as orf
+
+        orf.spectrum(x, self.nfft, "hann")
+
+    def cpu_rows_bytes(self, rows):
+        return 16 * rows * self.n
+
+
+class Fir:
+    """FIR filtering by overlap-save (the reference's rf.fir): 16 complex64 signals of 2^20 N(0, 1)
+    samples (2^24 points), 255 real taps, blocks of 1024 (default_nfft); one fused kernel (both
+    transforms and the product on chip). Bytes: 8 read + 8 written per sample (the overlap's
+    re-read, 254 of every 1024 samples, is not counted)."""
+
+    name = "rf.fir 255 taps nfft=1024 overlap-save, 16 x 2^20 c64 N(0,1)"
+
+    def __init__(self, impl: str, rows: int = 16, n: int = 1 << 20, taps: int = 255):
+        self.impl, self.rows, self.n, self.m = impl, rows, n, taps
+        self.nfft = 1024
+        self.bytes_per_call = 16 * rows * n
+
+    host_input = Spectrum.host_input
+
+    def device_sets(self, torch, seed):
+        from spectral import rf
+
+        rng = np.random.default_rng(seed + 100)
+        self.taps = torch.from_numpy((rng.standard_normal(self.m) / np.sqrt(self.m)).astype(np.float32)).cuda()
+        self.h = rf.taps_spectrum(self.taps, self.nfft, fft_impl=self.impl, device="cuda")
+        sets = []
+        for i in range(SETS):
+            x = torch.from_numpy(self.host_input(seed + i)).cuda()
+            sets.append((x, torch.empty_like(x)))
+        return sets
+
+    def kernels(self):
+        return [("fir", self.bytes_per_call)]
+
+    def launches_per_step(self) -> int:
+        return 1
+
+    def launch(self, native, sets, k, stream, which):
+        x, y = sets[k % SETS]
+        native.call("spectral_fir", self.impl.encode(), x.data_ptr(), self.h.data_ptr(), y.data_ptr(),
+                    self.n, self.nfft, self.m, self.rows, stream)
+
+    def api_step(self, spectral, x_dev):
+        from spectral import rf
+
+        return rf.fir(x_dev, self.taps, nfft=self.nfft, fft_impl=self.impl)
+
+    def io_bytes(self):
+        return 8 * self.rows * self.n, 8 * self.rows * self.n
+
+    def cpu_step(self, ref, x):
+        from oracle import rf as orf
+
+        rng = np.random.default_rng(1)
+        orf.fir_overlap_save(x, rng.standard_normal(self.m) / np.sqrt(self.m), self.nfft)
+
+    def cpu_rows_bytes(self, rows):
+        return 16 * rows * self.n
+
+
 class Slab:
     """one 16384 x 16384 complex64 field, N(0, 1) parts, slab-decomposed by rows over
     the ranks: row transforms, an NCCL all-to-all, column transforms (spectral.distributed).
@@ -428,6 +539,10 @@ def make_workload(args):
         return Rfft2(args.fft_impl, args.columns)
     if args.workload == "slab":
         return Slab(args.fft_impl)
+    if args.workload == "spectrum":
+        return Spectrum(args.fft_impl)
+    if args.workload == "fir":
+        return Fir(args.fft_impl)
     return Pruned(args.fft_impl)
 
 
@@ -560,7 +675,7 @@ def cpu_time(wl, rows: int, threads: int, reps: int) -> tuple[float, int]:
 
 
 def cpu_sample_rows(wl) -> int:
-    if isinstance(wl, Pruned):
+    if isinstance(wl, (Pruned, Spectrum, Fir)):
         return 4
     if isinstance(wl, Rfft2):
         return 64

@@ -440,6 +440,63 @@ at::Tensor mode_contract_cuda(const at::Tensor& x, const at::Tensor& w)
     return y;
 }
 
+// The fused radio-signal kernels behind spectral.rf: x is (..., n) complex64, each leading index
+// one signal. The Python layer picks these for the stockham implementations and nfft <= 4096.
+at::Tensor spectrum_frames_cuda(const at::Tensor& x, int64_t nfft, const c10::optional<at::Tensor>& window,
+                                c10::string_view impl_name)
+{
+    check_complex64_cuda(x, "x");
+    TORCH_CHECK(x.dim() >= 1, "spectrum: x needs at least one dimension");
+    const std::string impl(impl_name.data(), impl_name.size());
+    const int64_t n = x.size(-1);
+    int64_t rows = 1;  // the product of the leading dimensions (x may be empty)
+    for (int64_t d = 0; d + 1 < x.dim(); ++d) {
+        rows *= x.size(d);
+    }
+    TORCH_CHECK(nfft >= 2 && nfft <= 4096 && (nfft & (nfft - 1)) == 0,
+                "spectrum: nfft must be a power of two from 2 to 4096, got ", nfft);
+    const int64_t frames = n == 0 ? 1 : (n + nfft - 1) / nfft;
+    std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end() - 1);
+    shape.push_back(frames);
+    shape.push_back(nfft);
+    at::Tensor y = at::empty(shape, x.options());
+    at::Tensor wc;
+    if (window.has_value()) {
+        TORCH_CHECK(window->is_cuda() && window->scalar_type() == at::kFloat && window->dim() == 1
+                        && window->size(0) == nfft,
+                    "spectrum: the window must be a float32 CUDA tensor of nfft = ", nfft, " values");
+        wc = window->contiguous();
+    }
+    const c10::cuda::CUDAGuard guard(x.device());
+    const at::Tensor xc = contiguous_aligned(x);
+    check_status(spectral_spectrum(impl.c_str(), n == 0 ? nullptr : cptr(xc),
+                                   window.has_value() ? wc.const_data_ptr<float>() : nullptr, mptr(y), n,
+                                   static_cast<int>(nfft), rows, stream()));
+    return y;
+}
+
+at::Tensor fir_overlap_save_cuda(const at::Tensor& x, const at::Tensor& taps_spectrum, int64_t taps,
+                                 int64_t nfft, c10::string_view impl_name)
+{
+    check_complex64_cuda(x, "x");
+    check_complex64_cuda(taps_spectrum, "taps_spectrum");
+    TORCH_CHECK(x.dim() >= 1, "fir: x needs at least one dimension");
+    TORCH_CHECK(taps_spectrum.dim() == 1 && taps_spectrum.size(0) == nfft,
+                "fir: taps_spectrum must hold nfft = ", nfft, " values");
+    TORCH_CHECK(taps >= 1 && taps <= nfft, "fir: need 1 <= taps <= nfft");
+    const std::string impl(impl_name.data(), impl_name.size());
+    at::Tensor y = at::empty(x.sizes(), x.options());
+    const int64_t n = x.size(-1);
+    const int64_t rows = n == 0 ? 0 : x.numel() / n;
+    const c10::cuda::CUDAGuard guard(x.device());
+    const at::Tensor xc = contiguous_aligned(x);
+    const at::Tensor hc = contiguous_aligned(taps_spectrum);
+    check_status(spectral_fir(impl.c_str(), n == 0 ? nullptr : cptr(xc), cptr(hc),
+                              n == 0 ? nullptr : mptr(y), n, static_cast<int>(nfft),
+                              static_cast<int>(taps), rows, stream()));
+    return y;
+}
+
 // spectral._C.fft_impls(): the registry's names, in order, as a tuple of str.
 PyObject* py_fft_impls(PyObject*, PyObject*)
 {
@@ -481,6 +538,9 @@ TORCH_LIBRARY(spectral, m)
     m.def("rfft2_modes(Tensor x, int m1, int m2, str impl=\"naive\") -> Tensor");
     m.def("irfft2_modes(Tensor modes, int n1, int n2, str impl=\"naive\") -> Tensor");
     m.def("mode_contract(Tensor x, Tensor w) -> Tensor");
+    m.def("spectrum_frames(Tensor x, int nfft, Tensor? window=None, str impl=\"stockham_r8\") -> Tensor");
+    m.def("fir_overlap_save(Tensor x, Tensor taps_spectrum, int taps, int nfft, str impl=\"stockham_r8\")"
+          " -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(spectral, CUDA, m)
@@ -496,6 +556,8 @@ TORCH_LIBRARY_IMPL(spectral, CUDA, m)
     m.impl("rfft2_modes", &rfft2_modes_cuda);
     m.impl("irfft2_modes", &irfft2_modes_cuda);
     m.impl("mode_contract", &mode_contract_cuda);
+    m.impl("spectrum_frames", &spectrum_frames_cuda);
+    m.impl("fir_overlap_save", &fir_overlap_save_cuda);
 }
 
 PyMODINIT_FUNC PyInit__C(void)

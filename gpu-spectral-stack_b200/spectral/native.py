@@ -72,6 +72,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_ipc_close": (_i, [_p]),
     "spectral_ipc_free": (_i, [_p]),
     "spectral_mode_contract": (_i, [_p, _p, _p, _ll, _i, _i, _ll, _p]),
+    "spectral_spectrum": (_i, [_s, _p, _p, _p, _ll, _i, _ll, _p]),
+    "spectral_fir": (_i, [_s, _p, _p, _p, _ll, _i, _i, _ll, _p]),
 }
 
 

@@ -222,6 +222,27 @@ SPECTRAL_API int spectral_ipc_free(void* ptr);
 SPECTRAL_API int spectral_mode_contract(const void* x, const void* w, void* out, long long batch, int cin,
                            int cout, long long modes, void* stream);
 
+/* --- radio signals: windowed spectrum and overlap-save FIR (reference: python/spectral/rf.py) -- */
+
+/* Windowed spectrum of back-to-back frames (rf.py:94-102, spectrum): each of `rows` complex
+ * signals of n samples (x, rows * n values) is cut into frames = max(1, ceil(n / nfft)) frames
+ * of nfft samples, the last zero-padded; each frame is multiplied by `window` (nfft floats; NULL
+ * for the rectangular window) and transformed. y: rows * frames * nfft values. nfft a power of
+ * two from 2 to 4096; `impl` one of the stockham names (the others have no fused kernel). One
+ * kernel: framing, padding and window are applied in the transform's load. */
+SPECTRAL_API int spectral_spectrum(const char* impl, const void* x, const float* window, void* y, long long n,
+                                   int nfft, long long rows, void* stream);
+
+/* Causal FIR filter by overlap-save (rf.py:120-153, fir), y[j] = sum_k taps[k] x[j - k] with
+ * zero initial state, per row of n samples: blocks of nfft samples overlapping by taps - 1, each
+ * transformed, multiplied by taps_spectrum (the nfft-point forward transform of the taps zero-
+ * padded to nfft, e.g. from spectral_c2c), transformed back; the last nfft - taps + 1 outputs of
+ * each block are kept. x and y: rows * n values, not overlapping. nfft a power of two from
+ * max(2, taps) to 4096; `impl` one of the stockham names. One kernel: both transforms and the
+ * product run on chip. */
+SPECTRAL_API int spectral_fir(const char* impl, const void* x, const void* taps_spectrum, void* y, long long n,
+                              int nfft, int taps, long long rows, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

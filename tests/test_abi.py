@@ -73,6 +73,11 @@ def test_unknown_implementation_is_rejected_by_name():
          "1 <= m1 <= n1/2"),
         ("spectral_c2c_pruned", (b"stockham_r8", 0, 0, 8, 9, 1, 0, 0, None), "keep must be in"),
         ("spectral_c2c", (b"stockham_r8", 4096, 4096, 8, 2, 0, None), "must not overlap"),
+        ("spectral_spectrum", (b"stockham_r8", 0, 0, 0, 100, 12, 1, None), "power of two from 2 to 4096"),
+        ("spectral_spectrum", (b"naive", 0, 0, 0, 100, 64, 1, None), "no fused kernel"),
+        ("spectral_fir", (b"stockham_r8", 0, 0, 0, 100, 64, 65, 1, None), "at least len\\(taps\\) = 65"),
+        ("spectral_fir", (b"stockham_r8", 4096, 0, 4096, 100, 64, 8, 1, None), "must not overlap"),
+        ("spectral_fir", (b"stockham_r8", 0, 0, 0, 100, 8192, 8, 1, None), "power of two from 2 to 4096"),
     ],
 )
 def test_argument_checks_use_the_reference_messages(fn, args, message):
@@ -90,6 +95,8 @@ def test_argument_checks_use_the_reference_messages(fn, args, message):
         ("spectral_c2c", (b"stockham_r8", 4100, 8192, 8, 1, 0, None)),
         ("spectral_mode_contract", (4100, 8192, 16384, 1, 1, 1, 1, None)),
         ("spectral_slab_rows", (4100, 8192, 8, 8, 1, 0, None)),
+        ("spectral_spectrum", (b"stockham_r8", 4100, 0, 8192, 100, 64, 1, None)),
+        ("spectral_fir", (b"stockham_r8", 4096, 4100, 8192, 100, 64, 8, 1, None)),
     ],
 )
 def test_misaligned_arrays_are_refused_before_any_launch(fn, args):
@@ -119,7 +126,8 @@ def test_cpu_tensors_are_rejected_by_the_dispatcher():
 
 def test_every_operator_schema_is_registered():
     for op in ["scale", "fft_c2c", "fft_r2c", "fft_c2r", "fft2_c2c", "fft2_r2c", "fft2_c2r",
-               "fft_c2c_pruned", "rfft2_modes", "irfft2_modes", "mode_contract"]:
+               "fft_c2c_pruned", "rfft2_modes", "irfft2_modes", "mode_contract", "spectrum_frames",
+               "fir_overlap_save"]:
         assert hasattr(torch.ops.spectral, op), op
     schema = str(torch.ops.spectral.fft_c2c.default._schema)
     assert 'str impl="naive"' in schema and "bool inverse=False" in schema

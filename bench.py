@@ -1,7 +1,7 @@
 """Benchmark of the batched-FFT hot path: one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload real|c2c|rfft2|pruned|slab|spectrum|fir] [--fft-impl stockham_r8]
+                    [--workload real|c2c|rfft2|pruned|slab|spectrum|fir|flow] [--fft-impl stockham_r8]
 
 The headline workload is the one the metric is quoted on (configs[1] of BASELINE.json): a step
 is rfft then irfft of 4096 rows of 4096 float32 samples, iid U[-1, 1] from a seed, 2^24 points
@@ -59,7 +59,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=500)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["real", "c2c", "rfft2", "pruned", "slab", "spectrum", "fir"],
+    p.add_argument("--workload", choices=["real", "c2c", "rfft2", "pruned", "slab", "spectrum", "fir", "flow"],
                    default="real")
     p.add_argument("--fft-impl", default="stockham_r8", help="registry name (spectral.FFT_IMPLS)")
     p.add_argument("--columns", default="strided", help="rfft2 workload: strided or transpose")
@@ -530,6 +530,200 @@ def run_slab(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# --- the Navier-Stokes consumer ------------------------------------------------------------------
+
+FLOW_METRIC = "Navier-Stokes solver trajectory-steps/s, n=128 pruned, batch 256 (throughput.json)"
+FLOW_UNIT = "trajectory-steps/s"
+FLOW_PUBLISHED = 108682.0  # the reference's docs/results/throughput.json, stockham_r8 pruned, RTX 5080 Laptop
+
+
+def flow_setup(batch: int, n: int, seed: int):
+    """The throughput configuration of the reference's dataset params: n = 128, dt = 0.0025,
+    viscosity U[1e-3, 5e-3] per trajectory, drag 0.1, Kolmogorov forcing A = 1, k_f = 4; initial
+    vorticity smooth random fields of rms 5."""
+    rng = np.random.default_rng(seed)
+    nus = rng.uniform(1e-3, 5e-3, batch)
+    kx = np.arange(n // 2 + 1)[None, :]
+    k = np.arange(n)
+    ky = np.where(k < n // 2, k, k - n)[:, None]
+    spec = np.fft.rfft2(rng.standard_normal((batch, n, n))) * np.exp(-(kx**2 + ky**2) / 18.0)
+    spec[..., 0, 0] = 0
+    w0 = np.fft.irfft2(spec, s=(n, n))
+    w0 = (5.0 * w0 / w0.std(axis=(-2, -1), keepdims=True)).astype(np.float32)
+    return nus, w0
+
+
+def run_flow(args) -> None:
+    import torch
+
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "ours", "unavailable": "no CUDA device visible"}))
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    import spectral
+    from spectral.flow import Flow
+    from spectral.flow.gpu import GpuSolver
+
+    batch, n, dt = 256, 128, 0.0025
+    nus, w0 = flow_setup(batch, n, seed=1000 * rank + 1)
+    solver = GpuSolver(n, Flow(viscosity=nus, drag=0.1), dt, fft_impl=args.fft_impl, pruned=True)
+    w_hat = solver.to_spectral(torch.from_numpy(w0).cuda())
+    graph, state = solver._graph(w_hat)
+    state.copy_(w_hat)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # Timed: K steps, each its own event pair, with a write of 2x the L2 between steps (outside
+    # the events), so every step starts from HBM like a step of a long run with other work.
+    flush = torch.empty(2 * 126 * 2**20 // 4, dtype=torch.float32, device="cuda")
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for a, b in events:
+            flush.fill_(1.0)
+            a.record(stream)
+            graph.replay()
+            b.record(stream)
+        torch.cuda.synchronize()
+    step_ms = [a.elapsed_time(b) for a, b in events]
+    total_ms = sum(step_ms)
+    # Back to back (the solver's own loop): no flush between steps.
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    b2b_ms = s0.elapsed_time(s1)
+    t = torch.tensor([total_ms, b2b_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, b2b_ms = (float(v) for v in t.tolist())
+    value = world * batch * args.steps / (total_ms * 1e-3)
+
+    # The dominant kernel's roofline: the pruned inverse of the four fields, timed alone.
+    modes = torch.randn(4, batch, 2 * solver.spectral.m, solver.spectral.m, dtype=torch.complex64, device="cuda")
+    out = spectral.irfft2_from_modes(modes, (n, n), impl=args.fft_impl)
+    reps = 50
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for _ in range(reps):
+        spectral.irfft2_from_modes(modes, (n, n), impl=args.fft_impl)
+    k1.record(stream)
+    torch.cuda.synchronize()
+    inv_ms = k0.elapsed_time(k1) / reps
+    inv_bytes = modes.numel() * 8 + out.numel() * 4
+    peak, peak_source = hbm_peak()
+    achieved = inv_bytes / (inv_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": None, "kernel": "irfft2_modes (4 x 256 fields)",
+                "peak_source": f"{peak_source} (MEASURED_PEAKS.json hbm_gbs, copy)", "per_launch_us": round(1000 * inv_ms, 2)}
+
+    # End to end through the public API: pinned host vorticity in, to_spectral, 40 steps (one
+    # recorded frame of the reference's dataset params), to_physical, the frame back to the host.
+    e2e = None
+    if not args.no_e2e:
+        host_in = torch.from_numpy(w0).pin_memory()
+        host_out = torch.empty_like(host_in).pin_memory()
+        record_every = 40
+
+        def interval():
+            frames = solver.frames(host_in.cuda(non_blocking=True), record_every, record_every)
+            next(frames)
+            host_out.copy_(next(frames), non_blocking=True)
+
+        interval()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps_e = 5
+        e0.record(stream)
+        for _ in range(reps_e):
+            interval()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1) / reps_e
+        e2e = {"value": round(world * batch * record_every / (e_ms * 1e-3), 1), "unit": FLOW_UNIT,
+               "h2d_bytes_per_step": host_in.numel() * 4, "d2h_bytes_per_step": host_out.numel() * 4,
+               "steps": reps_e, "path": "GpuSolver.frames: host vorticity in, 40 steps, frame out",
+               "step": "one recorded frame interval (40 solver steps) of the reference's dataset params"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = flow_cpu(threads=os.cpu_count() or 1, trajectories=8, steps=4)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": FLOW_METRIC, "value": round(value, 1), "unit": FLOW_UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": round(value / world / FLOW_PUBLISHED, 2),
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "Navier-Stokes GpuSolver.step, 256 trajectories of 128x128, pruned (m=43), dt=0.0025, "
+                               "nu U[1e-3,5e-3], drag 0.1, Kolmogorov k_f=4", "fft_impl": args.fft_impl,
+                   "graph": "one CUDA graph per step", "l2": "2x L2 written between timed steps (outside the events)",
+                   "back_to_back_trajectory_steps_per_s": round(world * batch * args.steps / (b2b_ms * 1e-3), 1),
+                   "published_baseline": "108,682 trajectory-steps/s, stockham_r8 pruned, RTX 5080 Laptop GPU"},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": None, "clocks": clocks.summary(), "impl": "ours",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def flow_cpu(threads: int, trajectories: int, steps: int) -> dict:
+    """The reference's CPU solver (its float64 numpy flow/reference.py, restated as oracle/flow.py)
+    on `trajectories` of the workload's trajectories for `steps` steps, spread over `threads`."""
+    from oracle import flow as oflow
+
+    nus, w0 = flow_setup(trajectories, 128, seed=5)
+    chunks = [np.arange(trajectories)[i::threads] for i in range(min(threads, trajectories))]
+
+    def work(idx):
+        solver = oflow.Solver(128, 0.0025, viscosity=nus[idx], drag=0.1)
+        w = oflow.to_spectral(w0[idx], 128)
+        for _ in range(steps):
+            w = solver.step(w)
+
+    with ThreadPoolExecutor(max_workers=len(chunks)) as pool:
+        list(pool.map(work, chunks))  # warm-up
+        t0 = time.perf_counter()
+        list(pool.map(work, chunks))
+        t = time.perf_counter() - t0
+    return {"value": round(trajectories * steps / t, 2), "unit": FLOW_UNIT, "cores": len(chunks), "kind": "port",
+            "sample": f"{trajectories} trajectories x {steps} steps of the workload, float64 numpy solver"}
+
+
+def run_flow_reference(args) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    threads = os.cpu_count() or 1
+    per = []
+    for _ in range(max(1, args.steps)):
+        per.append(flow_cpu(threads, trajectories=min(64, 2 * threads), steps=2)["value"])
+    value = statistics.median(per)
+    line = {"impl": "reference", "metric": FLOW_METRIC, "value": value, "unit": FLOW_UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "Navier-Stokes step, 128x128, the reference's float64 numpy solver"},
+            "cpu_baseline": {"value": value, "unit": FLOW_UNIT, "cores": threads, "kind": "port",
+                             "sample": "min(64, 2 x cores) trajectories x 2 steps per measurement"},
+            "e2e": {"value": value, "unit": FLOW_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def make_workload(args):
     if args.workload == "real":
         return Real(args.fft_impl)
@@ -808,7 +1002,7 @@ def run_ours(args) -> None:
         def e2e_step(k: int) -> None:
             with torch.cuda.stream(lanes[k % 2]):
                 result = wl.api_step(spectral, hosts[k % 2].cuda(non_blocking=True))
-                outs[k % 2].copy_(result, non_blocking=True)
+                outs[k % 2].view(result.shape).copy_(result, non_blocking=True)
 
         for k in range(4):
             e2e_step(k)
@@ -872,7 +1066,9 @@ def run_ours(args) -> None:
 
 def main() -> None:
     args = parse()
-    if args.impl == "reference":
+    if args.workload == "flow":
+        (run_flow_reference if args.impl == "reference" else run_flow)(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "slab":
         run_slab(args)

@@ -497,6 +497,43 @@ at::Tensor fir_overlap_save_cuda(const at::Tensor& x, const at::Tensor& taps_spe
     return y;
 }
 
+// One stage of the Navier-Stokes step (spectral.flow.gpu): writes f0 (predictor) and out.
+void flow_stage_cuda(const at::Tensor& x, const at::Tensor& w, at::Tensor& f0, at::Tensor& out,
+                     const at::Tensor& derive, const at::Tensor& forcing, const at::Tensor& mask,
+                     const at::Tensor& explicit_factor, const at::Tensor& implicit_factor, at::Tensor& work,
+                     int64_t n, int64_t m, double dt, int64_t stage, c10::string_view impl_name)
+{
+    for (const at::Tensor* t : {&x, &w, const_cast<const at::Tensor*>(&f0), const_cast<const at::Tensor*>(&out),
+                                &derive, &forcing, const_cast<const at::Tensor*>(&work)}) {
+        check_complex64_cuda(*t, "flow_stage arrays");
+        TORCH_CHECK(t->is_contiguous(), "flow_stage: arrays must be contiguous");
+    }
+    for (const at::Tensor* t : {&mask, &explicit_factor, &implicit_factor}) {
+        TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous(),
+                    "flow_stage: mask and factors must be contiguous float32 CUDA tensors");
+    }
+    const int64_t plane = 2 * m * m;
+    TORCH_CHECK(x.numel() % plane == 0 && w.numel() == x.numel() && f0.numel() == x.numel() && out.numel() == x.numel(),
+                "flow_stage: states must be (batch, 2m, m)");
+    TORCH_CHECK(derive.numel() == 4 * plane && forcing.numel() == plane && mask.numel() == plane,
+                "flow_stage: derive (4, 2m, m), forcing and mask (2m, m)");
+    const int64_t batch = x.numel() / plane;
+    const int64_t vs = explicit_factor.numel() == plane ? 0 : plane;
+    TORCH_CHECK(explicit_factor.numel() == implicit_factor.numel()
+                    && (vs == 0 || explicit_factor.numel() == batch * plane),
+                "flow_stage: the factors must be (2m, m) or (batch, 2m, m)");
+    size_t count = 0;
+    check_status(spectral_flow_workspace(static_cast<int>(n), static_cast<int>(m), batch, &count));
+    TORCH_CHECK(static_cast<size_t>(work.numel()) >= count, "flow_stage: work needs ", count, " values");
+    const std::string impl(impl_name.data(), impl_name.size());
+    const c10::cuda::CUDAGuard guard(x.device());
+    check_status(spectral_flow_stage(impl.c_str(), cptr(x), cptr(w), mptr(f0), mptr(out), cptr(derive), cptr(forcing),
+                                     mask.const_data_ptr<float>(), explicit_factor.const_data_ptr<float>(),
+                                     implicit_factor.const_data_ptr<float>(), vs, mptr(work), static_cast<int>(n),
+                                     static_cast<int>(m), batch, static_cast<float>(dt), static_cast<int>(stage),
+                                     stream()));
+}
+
 // spectral._C.fft_impls(): the registry's names, in order, as a tuple of str.
 PyObject* py_fft_impls(PyObject*, PyObject*)
 {
@@ -541,6 +578,9 @@ TORCH_LIBRARY(spectral, m)
     m.def("spectrum_frames(Tensor x, int nfft, Tensor? window=None, str impl=\"stockham_r8\") -> Tensor");
     m.def("fir_overlap_save(Tensor x, Tensor taps_spectrum, int taps, int nfft, str impl=\"stockham_r8\")"
           " -> Tensor");
+    m.def("flow_stage(Tensor x, Tensor w, Tensor(a!) f0, Tensor(b!) out, Tensor derive, Tensor forcing, Tensor mask,"
+          " Tensor explicit_factor, Tensor implicit_factor, Tensor(c!) work, int n, int m, float dt, int stage,"
+          " str impl=\"stockham_r8\") -> ()");
 }
 
 TORCH_LIBRARY_IMPL(spectral, CUDA, m)
@@ -558,6 +598,7 @@ TORCH_LIBRARY_IMPL(spectral, CUDA, m)
     m.impl("mode_contract", &mode_contract_cuda);
     m.impl("spectrum_frames", &spectrum_frames_cuda);
     m.impl("fir_overlap_save", &fir_overlap_save_cuda);
+    m.impl("flow_stage", &flow_stage_cuda);
 }
 
 PyMODINIT_FUNC PyInit__C(void)

@@ -16,6 +16,12 @@ Each step evaluates the tendency F = f_hat - N_hat twice. One evaluation: the fo
 product u omega_x + v omega_y (two fused multiply-adds); one forward transform; the mask and the
 forcing. With graphs=True (the default on CUDA) a whole step is captured once per state shape
 as a CUDA graph and replayed, so a step costs one launch from the host instead of about thirty.
+
+For the pruned layout with a stockham implementation (16 <= n <= 512) a step is instead two
+stages of three fused kernels each (torch.ops.spectral.flow_stage, csrc/flow.cu): the derived
+spectra and the inverse column transforms; the four real row transforms, the product and the
+forward row transform; the forward column transforms with the mask, forcing and update. The
+physical fields then stay on chip, and the corrector updates the state in place.
 """
 
 from __future__ import annotations
@@ -113,6 +119,15 @@ class GpuSolver:
         self.implicit = (1.0 / (1.0 - 0.5 * dt * linear)).to(torch.complex64)
         self._graph_cache: dict[tuple, tuple] = {}
 
+        # The fused stages (pruned layout, stockham implementations): real factors, contiguous.
+        self.fused = (pruned and fft_impl.startswith("stockham") and 16 <= n <= 512
+                      and self.device.type == "cuda")
+        if self.fused:
+            self._mask = s.mask.expand(self.inverse_k2.shape).contiguous()
+            self._forcing = self.forcing_hat.contiguous()
+            self._explicit = (1.0 + 0.5 * dt * linear).to(torch.float32).contiguous()
+            self._implicit = (1.0 / (1.0 - 0.5 * dt * linear)).to(torch.float32).contiguous()
+
     def to_spectral(self, w: torch.Tensor) -> torch.Tensor:
         """omega_hat of physical vorticity (..., n, n), projected onto the dealiased modes."""
         return self.spectral.forward(w.to(torch.float32).contiguous()) * self.spectral.mask
@@ -127,7 +142,27 @@ class GpuSolver:
         nonlinear = torch.addcmul(u * wx, v, wy)
         return self.forcing_hat - self.spectral.forward(nonlinear) * self.spectral.mask
 
+    def _stage(self, x, w, f0, out, stage: int) -> None:
+        m = self.spectral.m
+        batch = w.numel() // (2 * m * m)
+        work = torch.empty(5 * batch * self.n * m, dtype=torch.complex64, device=w.device)
+        torch.ops.spectral.flow_stage.default(
+            x, w, f0, out, self.derive, self._forcing, self._mask, self._explicit, self._implicit, work,
+            self.n, m, self.dt, stage, self.spectral.fft_impl)
+
+    def _step_fused(self, w_hat: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """One step by the fused stages; out=w_hat updates the state in place."""
+        w = w_hat.contiguous()
+        f0 = torch.empty_like(w)
+        predicted = torch.empty_like(w)
+        out = torch.empty_like(w) if out is None else out
+        self._stage(w, w, f0, predicted, 0)
+        self._stage(predicted, w, f0, out, 1)
+        return out
+
     def _step_eager(self, w_hat: torch.Tensor) -> torch.Tensor:
+        if self.fused:
+            return self._step_fused(w_hat)
         f0 = self.tendency(w_hat)
         held = self.explicit * w_hat
         predicted = (held + self.dt * f0) * self.implicit
@@ -148,7 +183,10 @@ class GpuSolver:
             torch.cuda.current_stream(w_hat.device).wait_stream(side)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                state.copy_(self._step_eager(state))
+                if self.fused:
+                    self._step_fused(state, out=state)
+                else:
+                    state.copy_(self._step_eager(state))
             self._graph_cache[key] = (graph, state)
         return self._graph_cache[key]
 

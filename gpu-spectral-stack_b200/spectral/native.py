@@ -74,6 +74,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_mode_contract": (_i, [_p, _p, _p, _ll, _i, _i, _ll, _p]),
     "spectral_spectrum": (_i, [_s, _p, _p, _p, _ll, _i, _ll, _p]),
     "spectral_fir": (_i, [_s, _p, _p, _p, _ll, _i, _i, _ll, _p]),
+    "spectral_flow_workspace": (_i, [_i, _i, _ll, _szp]),
+    "spectral_flow_stage": (_i, [_s, _p, _p, _p, _p, _p, _p, _p, _p, _p, _ll, _p, _i, _i, _ll, _f, _i, _p]),
 }
 
 

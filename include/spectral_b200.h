@@ -243,6 +243,26 @@ SPECTRAL_API int spectral_spectrum(const char* impl, const void* x, const float*
 SPECTRAL_API int spectral_fir(const char* impl, const void* x, const void* taps_spectrum, void* y, long long n,
                               int nfft, int taps, long long rows, void* stream);
 
+/* --- the Navier-Stokes solver's step stage (reference: python/spectral/flow/gpu.py:115-129) ---- */
+
+/* One stage of the IMEX Crank-Nicolson / Heun step for `batch` vorticity spectra of an n x n grid
+ * (n a power of two, 16 .. 512) in the pruned layout: 2m rows (ky = 0 .. m-1, then -m .. -1) by
+ * m columns (kx = 0 .. m-1), complex values, 2 m <= n. With F(s) = forcing - mask * rfft2(u wx +
+ * v wy) the dealiased tendency of state s (u, v, wx, wy the inverse transforms of s times the four
+ * `derive` tables (4, 2m, m): i ky / |k|^2, -i kx / |k|^2, i kx, i ky):
+ *   stage 0 (predictor): f0 = F(x),  out = (E w + dt f0) I          (x is w)
+ *   stage 1 (corrector): out = (E w + dt/2 (f0 + F(x))) I           (x is the predictor's out)
+ * forcing (2m, m) complex; mask (2m, m), explicit_factor E and implicit_factor I ((2m, m) or one
+ * (2m, m) plane per trajectory: visc_stride 0 or 2 m m) float. out may be w for the corrector.
+ * `work` holds spectral_flow_workspace() complex values. Three kernels, no physical field in
+ * global memory; `impl` one of the stockham names. */
+SPECTRAL_API int spectral_flow_workspace(int n, int m, long long batch, size_t* count);
+SPECTRAL_API int spectral_flow_stage(const char* impl, const void* x, const void* w, void* f0, void* out,
+                                     const void* derive, const void* forcing, const float* mask,
+                                     const float* explicit_factor, const float* implicit_factor,
+                                     long long visc_stride, void* work, int n, int m, long long batch,
+                                     float dt, int stage, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

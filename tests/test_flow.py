@@ -202,3 +202,67 @@ def test_step_is_functional_and_frames_stream(rng):
     a = solver.step(w_hat)
     b = solver.step(w_hat)
     assert torch.equal(w_hat, before) and torch.equal(a, b)
+
+
+# --- the fused stages --------------------------------------------------------------------------
+
+
+@pytest.mark.gpu
+def test_fused_stages_are_used_for_the_pruned_stockham_layouts():
+    from spectral.flow import Flow
+    from spectral.flow.gpu import GpuSolver
+
+    assert GpuSolver(128, Flow(), 0.01, fft_impl="stockham_r8", pruned=True).fused
+    assert not GpuSolver(128, Flow(), 0.01, fft_impl="stockham_r8", pruned=False).fused
+    assert not GpuSolver(128, Flow(), 0.01, fft_impl="cufft", pruned=True).fused
+    assert not GpuSolver(1024, Flow(), 0.01, fft_impl="stockham_r8", pruned=True).fused
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("impl", ["stockham_r2", "stockham_r4", "stockham_r8", "stockham_r8_table"])
+@pytest.mark.parametrize("n", [16, 32, 128, 512])
+def test_fused_step_matches_the_composed_step(rng, impl, n):
+    # The same step through the composed path (separate transforms and elementwise passes) and
+    # through the three fused kernels per stage: equal to float32 rounding.
+    from spectral.flow import Flow
+    from spectral.flow.gpu import GpuSolver
+
+    nus = np.array([1e-3, 3e-3])
+    flow = Flow(viscosity=nus, drag=0.1)
+    fused = GpuSolver(n, flow, 2e-3, fft_impl=impl, pruned=True, graphs=False)
+    composed = GpuSolver(n, flow, 2e-3, fft_impl=impl, pruned=True, graphs=False)
+    composed.fused = False
+    w = torch.as_tensor(5 * oflow.smooth_random_field(rng, n, batch=(2,)), dtype=torch.float32, device="cuda")
+    a = fused.to_spectral(w)
+    b = a.clone()
+    for _ in range(10):
+        a, b = fused.step(a), composed.step(b)
+    assert relative(a.cpu().numpy(), b.cpu().numpy()) < 2e-6
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [16, 256])
+def test_fused_solver_agrees_with_the_oracle_at_the_size_limits(rng, n):
+    from spectral.flow import Flow
+
+    w0 = oflow.smooth_random_field(rng, n)
+    gpu = run(w0, Flow(viscosity=2e-3, drag=0.1), 4e-3, 50, "stockham_r8", True)
+    cpu = oflow.simulate(w0, 4e-3, 50, record_every=50, viscosity=2e-3, drag=0.1)
+    assert relative(gpu[-1], cpu[-1]) < 1e-4
+
+
+def test_flow_stage_argument_checks():
+    from spectral import native
+
+    with pytest.raises(ValueError, match="power of two from 16 to 512"):
+        native.workspace("spectral_flow_workspace", 48, 17, 2)
+    with pytest.raises(ValueError, match="1 <= m <= n/2"):
+        native.workspace("spectral_flow_workspace", 32, 17, 2)
+    assert native.workspace("spectral_flow_workspace", 128, 43, 256) == 5 * 256 * 128 * 43
+    args = [0] * 9 + [0, 0, 128, 43, 1, 0.01, 0, None]
+    with pytest.raises(ValueError, match="no fused kernels for implementation 'naive'"):
+        native.call("spectral_flow_stage", b"naive", 8, 16, 24, 32, *args[4:9], *args[9:])
+    with pytest.raises(ValueError, match="must not be x"):
+        native.call("spectral_flow_stage", b"stockham_r8", 8, 16, 24, 8, *args[4:9], *args[9:])
+    with pytest.raises(ValueError, match="stage must be 0"):
+        native.call("spectral_flow_stage", b"stockham_r8", 8, 16, 24, 32, *args[4:9], 0, 0, 128, 43, 1, 0.01, 2, None)

@@ -613,23 +613,36 @@ def run_flow(args) -> None:
     total_ms, b2b_ms = (float(v) for v in t.tolist())
     value = world * batch * args.steps / (total_ms * 1e-3)
 
-    # The dominant kernel's roofline: the pruned inverse of the four fields, timed alone.
-    modes = torch.randn(4, batch, 2 * solver.spectral.m, solver.spectral.m, dtype=torch.complex64, device="cuda")
-    out = spectral.irfft2_from_modes(modes, (n, n), impl=args.fft_impl)
-    reps = 50
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    k0.record(stream)
-    for _ in range(reps):
-        spectral.irfft2_from_modes(modes, (n, n), impl=args.fft_impl)
-    k1.record(stream)
-    torch.cuda.synchronize()
-    inv_ms = k0.elapsed_time(k1) / reps
-    inv_bytes = modes.numel() * 8 + out.numel() * 4
-    peak, peak_source = hbm_peak()
-    achieved = inv_bytes / (inv_ms * 1e-3) / 1e9
-    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": None, "kernel": "irfft2_modes (4 x 256 fields)",
-                "peak_source": f"{peak_source} (MEASURED_PEAKS.json hbm_gbs, copy)", "per_launch_us": round(1000 * inv_ms, 2)}
+    # Roofline of one stage (the step is two): the three fused kernels against HBM, with the
+    # bytes they move through global memory (the Y and Z intermediates included, though at this
+    # size they stay in the L2), timed alone with events.
+    roofline = None
+    if solver.fused:
+        m = solver.spectral.m
+        f0 = torch.empty_like(state)
+        scratch = torch.empty_like(state)
+        reps = 50
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        solver._stage(state, state, f0, scratch, 0)
+        k0.record(stream)
+        for _ in range(reps):
+            solver._stage(state, state, f0, scratch, 0)
+        k1.record(stream)
+        torch.cuda.synchronize()
+        stage_ms = k0.elapsed_time(k1) / reps
+        plane = 2 * m * m * 8  # bytes of one state
+        inter = n * m * 8      # bytes of one field's column-transformed intermediate
+        stage_bytes = batch * (plane + 4 * inter        # derive: the state in, Y out
+                               + 4 * inter + inter      # product: Y in, Z out
+                               + inter + 3 * plane)     # update: Z and the state in, f0 and out
+        peak, peak_source = hbm_peak()
+        achieved = stage_bytes / (stage_ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "traffic": None,
+                    "kernel": "flow_stage (derive columns + product rows + update columns)",
+                    "peak_source": f"{peak_source} (MEASURED_PEAKS.json hbm_gbs, copy)",
+                    "per_launch_us": round(1000 * stage_ms, 2), "bytes_per_launch": stage_bytes,
+                    "note": "latency/FP32-bound: the intermediates are L2-resident at this size"}
 
     # End to end through the public API: pinned host vorticity in, to_spectral, 40 steps (one
     # recorded frame of the reference's dataset params), to_physical, the frame back to the host.

@@ -246,11 +246,12 @@ template <int N, int B, bool Table>
 void run_stage(const StageArgs& a, cudaStream_t s)
 {
     constexpr int M = N / 2;
-    using CP = ColumnPlan<N>;
+    // Register budgets for occupancy: the column stages are latency-bound loops over small
+    // columns (up to n = 128: 64 registers, 8 CTAs of 128 threads per SM); the product stage
+    // holds three rows of registers (up to n = 256: two CTAs per SM). At n = 128 nothing spills.
+    using CP = Plan<N, default_e(N), false, default_threads(N), (N <= 128 ? 8 : N == 256 ? 3 : 1)>;
     constexpr RowChoice rc = row_choice(RowKind::C2r, M);
-    // The product kernel holds three rows of registers; rows of 128 points and more get the
-    // register budget of two CTAs per SM instead of four (no spills).
-    using RP = Plan<M, default_e(M), false, rc.threads, (M >= 128 ? 2 : rc.min_blocks)>;
+    using RP = Plan<M, default_e(M), false, rc.threads, (M <= 128 ? 2 : 1)>;
     const long long fields = 4 * a.batch;
     float2* y = a.work;
     float2* z = a.work + fields * N * a.m;

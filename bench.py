@@ -638,8 +638,8 @@ def run_flow(args) -> None:
         peak, peak_source = hbm_peak()
         achieved = stage_bytes / (stage_ms * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(achieved / peak, 4), "traffic": None,
-                    "kernel": "flow_stage (derive columns + product rows + update columns)",
+                    "frac": round(achieved / peak, 4), "traffic": ncu_traffic("flow_stage", "flow"),
+                    "kernel": "flow_stage", "kernels": "derive columns + product rows + update columns",
                     "peak_source": f"{peak_source} (MEASURED_PEAKS.json hbm_gbs, copy)",
                     "per_launch_us": round(1000 * stage_ms, 2), "bytes_per_launch": stage_bytes,
                     "note": "latency/FP32-bound: the intermediates are L2-resident at this size"}

@@ -65,6 +65,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--columns", default="strided", help="rfft2 workload: strided or transpose")
     p.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                    help="slab workload on 2+ GPUs: row kernel stores into the peers' memory, or an NCCL all-to-all")
+    p.add_argument("--layout", choices=["columns", "natural"], default="columns",
+                   help="slab workload: leave the column slab (one exchange) or return natural rows (two)")
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     return p.parse_args()
@@ -471,8 +473,13 @@ def run_slab(args) -> None:
     xs = [torch.complex(torch.randn(rows, n, device="cuda", generator=g),
                         torch.randn(rows, n, device="cuda", generator=g)) for _ in range(2)]
     stream = torch.cuda.current_stream()
-    peer = PeerSlab(n) if world > 1 and args.exchange == "peer" else None
-    transform = peer.forward if peer is not None else fft2_slab
+    natural = args.layout == "natural"
+    peer = PeerSlab(n, natural=natural) if world > 1 and args.exchange == "peer" else None
+    if peer is not None:
+        transform = peer.forward_natural if natural else peer.forward
+    else:
+        def transform(x):
+            return fft2_slab(x, layout=args.layout)
     for k in range(args.warmup):
         transform(xs[k % 2])
     torch.cuda.synchronize()
@@ -505,16 +512,18 @@ def run_slab(args) -> None:
     step_s = max_ms / args.steps * 1e-3
     # The bound: two passes (rows, columns) over the rank's slab, each reading and writing it,
     # against the all-to-all's bytes leaving each GPU at the measured 770 GB/s per direction.
+    # The natural layout adds a relayout pass and a second exchange.
     slab_bytes = 8 * n * n / world
-    hbm_s = 2 * 2 * slab_bytes / (peak * 1e9)
-    link_s = slab_bytes * (world - 1) / world / 770e9
+    passes, exchanges = (3, 2) if args.layout == "natural" and world > 1 else (2, 1)
+    hbm_s = passes * 2 * slab_bytes / (peak * 1e9)
+    link_s = exchanges * slab_bytes * (world - 1) / world / 770e9
     bound_s = max(hbm_s, link_s)
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": wl.name, "ranks": world, "rows_per_rank": rows,
+        "config": {"workload": wl.name, "ranks": world, "rows_per_rank": rows, "layout": args.layout,
                    "exchange": ("none (1 rank)" if world == 1 else
                                 "row kernel stores into the peers' buffers over NVLink (CUDA IPC), one all-reduce barrier"
                                 if peer is not None else "torch.distributed all_to_all_single (NCCL)")},

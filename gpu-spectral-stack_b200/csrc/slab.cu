@@ -308,6 +308,46 @@ void slab_columns(float2* x, float2* y, int n, int w, cudaStream_t s)
     });
 }
 
+// Block relayout between the column-slab side and the natural (row) side of the exchange: for
+// every rank r, the w x w block at src[r] (row stride src_stride) is copied to dst[r] (row stride
+// dst_stride). With the blocks' pointers chosen by the caller this is each of the four steps a
+// natural-layout transform needs:
+//   forward, received blocks -> rows:  src[r] = recv + r w^2 (w),  dst[r] = out + r w (n)
+//   inverse, rows -> send blocks:      src[r] = x + r w (n),       dst[r] = send + r w^2 (w)
+//   and the same with src[r] in another rank's memory (peer loads over NVLink, plain loads).
+// One thread moves two complex values (16 bytes) where w is even, so every warp reads and
+// writes runs of 512 bytes.
+constexpr int kMaxRelayoutRanks = 16;
+
+struct BlockTable {
+    const float2* src[kMaxRelayoutRanks];
+    float2* dst[kMaxRelayoutRanks];
+};
+
+template <bool Pairs>
+__global__ void __launch_bounds__(256) slab_relayout_kernel(const BlockTable t, int w, long long src_stride,
+                                                            long long dst_stride, long long per_rank)
+{
+    wait_for_previous_grid();
+    allow_next_grid();
+    constexpr int V = Pairs ? 2 : 1;
+    const int cols = w / V;  // vectors per block row
+    const int r = blockIdx.y;
+    const float2* src = t.src[r];
+    float2* dst = t.dst[r];
+    for (long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; e < per_rank;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long k = e / cols;
+        const int c = static_cast<int>(e - k * cols) * V;
+        if constexpr (Pairs) {
+            const float4 v = *reinterpret_cast<const float4*>(src + k * src_stride + c);
+            *reinterpret_cast<float4*>(dst + k * dst_stride + c) = v;
+        } else {
+            dst[k * dst_stride + c] = src[k * src_stride + c];
+        }
+    }
+}
+
 void check_aligned(const void* p)
 {
     if ((reinterpret_cast<unsigned long long>(p) & 7u) != 0) {
@@ -410,6 +450,45 @@ extern "C" int spectral_slab_rows_peer(const void* x, void* y, void* const* peer
             slab_rows<false>(n, rows, s, [&](float sc) {
                 return SlabPeerRowIo<false>{xs, nullptr, ps, rows, rank, wlog, sc};
             });
+        }
+    });
+}
+
+extern "C" int spectral_slab_relayout(const void* const* src, void* const* dst, int ranks, int w,
+                                      long long src_stride, long long dst_stride, void* stream)
+{
+    using namespace spectral;
+    return slab_guarded([&] {
+        if (ranks < 1 || ranks > kMaxRelayoutRanks) {
+            throw InvalidArgument("slab_relayout: ranks must be from 1 to " + std::to_string(kMaxRelayoutRanks));
+        }
+        if (w < 1 || src_stride < w || dst_stride < w) {
+            throw InvalidArgument("slab_relayout: need w >= 1 and row strides of at least w");
+        }
+        if (src == nullptr || dst == nullptr) {
+            throw InvalidArgument("slab_relayout: src and dst must list one block per rank");
+        }
+        BlockTable t = {};
+        bool pairs = w % 2 == 0 && src_stride % 2 == 0 && dst_stride % 2 == 0;
+        for (int r = 0; r < ranks; ++r) {
+            if (src[r] == nullptr || dst[r] == nullptr) {
+                throw InvalidArgument("slab_relayout: block " + std::to_string(r) + " is null");
+            }
+            check_aligned(src[r]);
+            check_aligned(dst[r]);
+            pairs = pairs && (reinterpret_cast<unsigned long long>(src[r]) & 15u) == 0
+                    && (reinterpret_cast<unsigned long long>(dst[r]) & 15u) == 0;
+            t.src[r] = static_cast<const float2*>(src[r]);
+            t.dst[r] = static_cast<float2*>(dst[r]);
+        }
+        const long long per_rank = static_cast<long long>(w) * (pairs ? w / 2 : w);
+        const long long blocks_x = (per_rank + 255) / 256;
+        const dim3 grid(static_cast<unsigned>(blocks_x < 4096 ? blocks_x : 4096), static_cast<unsigned>(ranks));
+        const auto s = static_cast<cudaStream_t>(stream);
+        if (pairs) {
+            launch_pdl(slab_relayout_kernel<true>, grid, dim3(256), 0, s, t, w, src_stride, dst_stride, per_rank);
+        } else {
+            launch_pdl(slab_relayout_kernel<false>, grid, dim3(256), 0, s, t, w, src_stride, dst_stride, per_rank);
         }
     });
 }

@@ -9,7 +9,13 @@ holds rows [r n/R, (r+1) n/R). The forward transform runs
 
 and returns the rank's w columns of the 2D transform, as an (n, w) tensor in natural order:
 element [k1, c] is X[k1, r w + c]. The inverse takes that column slab back to the rank's rows of
-ifft2 (divided by n^2). The reference cannot run this case (its fft2 stops at 4096 per side and it
+ifft2 (divided by n^2).
+
+layout="natural" adds the second exchange: the column slab's w x w row blocks go to the ranks
+that own those output rows, and a relayout kernel (spectral_slab_relayout) assembles the rank's
+rows [r w, (r+1) w) of fft2 as a (w, n) tensor, the layout of the input. The natural inverse
+starts from those rows: the relayout packs the send blocks, and the exchange delivers the column
+slab the plain inverse takes. The reference cannot run this case (its fft2 stops at 4096 per side and it
 has no multi-GPU code); batched transforms need no communication and use the plain operators.
 
 The kernel steps are arguments, so the index arithmetic of the decomposition can be tested on
@@ -48,6 +54,32 @@ def columns_kernel(x: torch.Tensor, n: int, width: int, inverse: bool) -> torch.
     return y
 
 
+def relayout_kernel(src: torch.Tensor, dst: torch.Tensor, ranks: int, w: int, src_offsets, src_stride: int,
+                    dst_offsets, dst_stride: int) -> None:
+    """Copies, for each rank r, the w x w block of src at element offset src_offsets[r] (row stride
+    src_stride) to dst at dst_offsets[r] (row stride dst_stride), complex64 on one device."""
+    table = ctypes.c_void_p * ranks
+    sp = table(*[src.data_ptr() + 8 * o for o in src_offsets])
+    dp = table(*[dst.data_ptr() + 8 * o for o in dst_offsets])
+    native.call("spectral_slab_relayout", sp, dp, ranks, w, src_stride, dst_stride, _stream())
+
+
+def _blocks_to_rows(recv: torch.Tensor, ranks: int, w: int, relayout_fn) -> torch.Tensor:
+    """(ranks, w, w) received blocks -> (w, ranks w): out[k, r w + c] = recv[r, k, c]."""
+    n = ranks * w
+    out = torch.empty((w, n), dtype=torch.complex64, device=recv.device)
+    relayout_fn(recv, out, ranks, w, [r * w * w for r in range(ranks)], w, [r * w for r in range(ranks)], n)
+    return out
+
+
+def _rows_to_blocks(x: torch.Tensor, ranks: int, w: int, relayout_fn) -> torch.Tensor:
+    """(w, ranks w) rows -> (ranks, w, w) send blocks: send[r, k, c] = x[k, r w + c]."""
+    n = ranks * w
+    send = torch.empty((ranks, w, w), dtype=torch.complex64, device=x.device)
+    relayout_fn(x, send, ranks, w, [r * w for r in range(ranks)], n, [r * w * w for r in range(ranks)], w)
+    return send
+
+
 def _world(group) -> tuple[int, int]:
     if dist.is_available() and dist.is_initialized():
         return dist.get_world_size(group), dist.get_rank(group)
@@ -68,14 +100,31 @@ def fft2_slab(
     *,
     inverse: bool = False,
     group=None,
+    layout: str = "columns",
     rows_fn: Callable = rows_kernel,
     columns_fn: Callable = columns_kernel,
+    relayout_fn: Callable = relayout_kernel,
 ) -> torch.Tensor:
-    """Forward: x is this rank's (n / R, n) row slab; returns its (n, n / R) column slab of fft2.
-    Inverse: x is the (n, n / R) column slab; returns the (n / R, n) row slab of ifft2."""
+    """Forward: x is this rank's (n / R, n) row slab; returns its (n, n / R) column slab of fft2,
+    or with layout="natural" its (n / R, n) rows of fft2. Inverse: x is the (n, n / R) column
+    slab (layout="natural": the (n / R, n) rows of the spectrum); returns the (n / R, n) row slab
+    of ifft2."""
     ranks, _ = _world(group)
     if x.dtype != torch.complex64 or x.dim() != 2:
         raise ValueError("fft2_slab: x must be a 2D complex64 tensor")
+    if layout not in ("columns", "natural"):
+        raise ValueError(f"fft2_slab: layout must be 'columns' or 'natural', got {layout!r}")
+    if layout == "natural":
+        w, n = x.shape
+        if w * ranks != n:
+            raise ValueError(f"fft2_slab: {ranks} ranks of {w} rows do not make a {n} x {n} field")
+        kw = dict(group=group, rows_fn=rows_fn, columns_fn=columns_fn, relayout_fn=relayout_fn)
+        if not inverse:
+            cols = fft2_slab(x, **kw)                                       # (n, w) = (ranks, w, w)
+            received = _exchange(cols.reshape(ranks, w, w), group)
+            return _blocks_to_rows(received, ranks, w, relayout_fn)
+        received = _exchange(_rows_to_blocks(x.contiguous(), ranks, w, relayout_fn), group)
+        return fft2_slab(received.reshape(n, w), inverse=True, **kw)
     if not inverse:
         rows, n = x.shape
         if rows * ranks != n:
@@ -104,9 +153,16 @@ class PeerSlab:
 
     Usage (every rank, same order): plan = PeerSlab(n); cols = plan.forward(rows);
     rows = plan.inverse(cols); plan.close().
+
+    natural=True adds the second exchange, again through peer memory: forward_natural returns the
+    rank's (n / R, n) rows of fft2 and inverse_natural takes them. The column transforms write the
+    column slab into a second pair of shared buffers, and the relayout kernel builds the rank's
+    rows by loading its w x w block from every rank's slab over NVLink. The inverse stages the
+    rows in that buffer and gathers the column slab the same way. Each direction adds one
+    barrier and no separate exchange pass.
     """
 
-    def __init__(self, n: int, group=None):
+    def __init__(self, n: int, group=None, natural: bool = False):
         ranks, rank = _world(group)
         if n % ranks:
             raise ValueError(f"PeerSlab: {ranks} ranks do not divide n = {n}")
@@ -118,29 +174,36 @@ class PeerSlab:
         self._local: list[int] = []
         self._opened: list[int] = []
         self._peers = []
-        lib = native.lib()
-        nbytes = 8 * n * self.w
-        for _ in range(2):
-            ptr = ctypes.c_void_p()
-            handle = ctypes.create_string_buffer(64)
-            native.check(lib.spectral_ipc_alloc(nbytes, ctypes.byref(ptr), handle))
-            self._local.append(ptr.value)
-            handles = [None] * ranks
-            if ranks > 1:
-                dist.all_gather_object(handles, handle.raw, group=group)
-            else:
-                handles[0] = handle.raw
-            table = (ctypes.c_void_p * ranks)()
-            for q in range(ranks):
-                if q == rank:
-                    table[q] = ptr.value
-                else:
-                    mapped = ctypes.c_void_p()
-                    native.check(lib.spectral_ipc_open(handles[q], ctypes.byref(mapped)))
-                    self._opened.append(mapped.value)
-                    table[q] = mapped.value
-            self._peers.append(table)
+        self.natural = natural
+        # Buffers 0, 1: the receive slabs of the row exchange; 2, 3 (natural only): the column
+        # slabs (forward) and staged rows (inverse) of the second exchange.
+        for _ in range(4 if natural else 2):
+            self._peers.append(self._shared(8 * n * self.w))
         self._barrier()
+
+    def _shared(self, nbytes: int):
+        """Allocates one buffer per rank through CUDA IPC; returns every rank's address in this
+        process (this rank's own, the others' mapped)."""
+        lib = native.lib()
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        native.check(lib.spectral_ipc_alloc(nbytes, ctypes.byref(ptr), handle))
+        self._local.append(ptr.value)
+        handles = [None] * self.ranks
+        if self.ranks > 1:
+            dist.all_gather_object(handles, handle.raw, group=self.group)
+        else:
+            handles[0] = handle.raw
+        table = (ctypes.c_void_p * self.ranks)()
+        for q in range(self.ranks):
+            if q == self.rank:
+                table[q] = ptr.value
+            else:
+                mapped = ctypes.c_void_p()
+                native.check(lib.spectral_ipc_open(handles[q], ctypes.byref(mapped)))
+                self._opened.append(mapped.value)
+                table[q] = mapped.value
+        return table
 
     def _barrier(self) -> None:
         if self.ranks > 1:
@@ -156,26 +219,65 @@ class PeerSlab:
         if x.shape != (self.rows, self.n) or x.dtype != torch.complex64:
             raise ValueError(f"PeerSlab.forward: x must be ({self.rows}, {self.n}) complex64")
         b = self._next()
+        out = torch.empty((self.n, self.w), dtype=torch.complex64, device=x.device)
+        self._forward(x, b, out.data_ptr())
+        return out
+
+    def _forward(self, x: torch.Tensor, b: int, out_ptr: int) -> None:
         x = x.contiguous()
         native.call("spectral_slab_rows_peer", x.data_ptr(), None, self._peers[b], self.n,
                     self.rows, self.rank, self.ranks, 0, _stream())
         self._barrier()
-        out = torch.empty((self.n, self.w), dtype=torch.complex64, device=x.device)
         # The received slab is this call's scratch: nobody writes it again before two calls on.
-        native.call("spectral_slab_columns", self._local[b], out.data_ptr(), self.n, self.w, 0,
+        native.call("spectral_slab_columns", self._peers[b][self.rank], out_ptr, self.n, self.w, 0,
                     _stream())
+
+    def forward_natural(self, x: torch.Tensor) -> torch.Tensor:
+        """x: this rank's (n / R, n) rows; returns its (n / R, n) rows of fft2."""
+        if not self.natural:
+            raise ValueError("PeerSlab.forward_natural: the plan was made without natural=True")
+        if x.shape != (self.rows, self.n) or x.dtype != torch.complex64:
+            raise ValueError(f"PeerSlab.forward_natural: x must be ({self.rows}, {self.n}) complex64")
+        b = self._next()
+        slabs = self._peers[2 + b]
+        self._forward(x, b, slabs[self.rank])
+        self._barrier()
+        out = torch.empty((self.w, self.n), dtype=torch.complex64, device=x.device)
+        w = self.w
+        src = (ctypes.c_void_p * self.ranks)(*[slabs[r] + 8 * self.rank * w * w for r in range(self.ranks)])
+        dst = (ctypes.c_void_p * self.ranks)(*[out.data_ptr() + 8 * r * w for r in range(self.ranks)])
+        native.call("spectral_slab_relayout", src, dst, self.ranks, w, w, self.n, _stream())
         return out
+
+    def inverse_natural(self, x: torch.Tensor) -> torch.Tensor:
+        """x: this rank's (n / R, n) rows of the spectrum; returns its (n / R, n) rows of ifft2."""
+        if not self.natural:
+            raise ValueError("PeerSlab.inverse_natural: the plan was made without natural=True")
+        if x.shape != (self.w, self.n) or x.dtype != torch.complex64:
+            raise ValueError(f"PeerSlab.inverse_natural: x must be ({self.w}, {self.n}) complex64")
+        b = self._next()
+        staged = self._peers[2 + b]
+        x = x.contiguous()
+        native.call("spectral_scale", x.data_ptr(), staged[self.rank], x.numel(), 1.0, _stream())
+        self._barrier()
+        w = self.w
+        cols = torch.empty((self.n, w), dtype=torch.complex64, device=x.device)
+        src = (ctypes.c_void_p * self.ranks)(*[staged[r] + 8 * self.rank * w for r in range(self.ranks)])
+        dst = (ctypes.c_void_p * self.ranks)(*[cols.data_ptr() + 8 * r * w * w for r in range(self.ranks)])
+        native.call("spectral_slab_relayout", src, dst, self.ranks, w, self.n, w, _stream())
+        return self._inverse(cols, b)
 
     def inverse(self, cols: torch.Tensor) -> torch.Tensor:
         """cols: the (n, n / R) column slab; returns this rank's (n / R, n) rows of ifft2."""
         if cols.shape != (self.n, self.w) or cols.dtype != torch.complex64:
             raise ValueError(f"PeerSlab.inverse: cols must be ({self.n}, {self.w}) complex64")
-        b = self._next()
-        scratch = cols.contiguous().clone()
-        native.call("spectral_slab_columns", scratch.data_ptr(), self._local[b], self.n, self.w, 1,
+        return self._inverse(cols.contiguous().clone(), self._next())
+
+    def _inverse(self, scratch: torch.Tensor, b: int) -> torch.Tensor:
+        native.call("spectral_slab_columns", scratch.data_ptr(), self._peers[b][self.rank], self.n, self.w, 1,
                     _stream())
         self._barrier()
-        y = torch.empty((self.rows, self.n), dtype=torch.complex64, device=cols.device)
+        y = torch.empty((self.rows, self.n), dtype=torch.complex64, device=scratch.device)
         native.call("spectral_slab_rows_peer", None, y.data_ptr(), self._peers[b], self.n,
                     self.rows, self.rank, self.ranks, 1, _stream())
         return y

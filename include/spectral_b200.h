@@ -184,6 +184,17 @@ SPECTRAL_API int spectral_slab_rows_peer(const void* x, void* y, void* const* pe
                                          long long rows, int rank, int ranks, int inverse,
                                          void* stream);
 
+/* Natural layout. The column slab leaves rank r with output columns [r w, (r+1) w); a second
+ * exchange of its w x w row blocks returns rows [r w, (r+1) w) of the transform instead. This
+ * entry point copies, for each rank r (at most 16), the w x w block at src[r] (row stride
+ * src_stride complex values) to dst[r] (row stride dst_stride). After the exchange of the column
+ * slab's row blocks, src[r] = recv + r w^2 (stride w) and dst[r] = out + r w (stride n) give
+ * the natural w x n rows. Before an inverse, src[r] = x + r w (stride n) and dst[r] = send +
+ * r w^2 (stride w) pack the send blocks. src[r] may be another rank's buffer mapped through
+ * CUDA IPC (plain NVLink loads), which fuses the exchange into the copy. */
+SPECTRAL_API int spectral_slab_relayout(const void* const* src, void* const* dst, int ranks, int w,
+                                        long long src_stride, long long dst_stride, void* stream);
+
 /* The whole slab transform through the C ABI, with the exchange on an NCCL communicator given as
  * void* (ncclComm_t; no counterpart in the reference). Forward: x is this rank's n/ranks rows
  * (rows x n), y receives its n x n/ranks column slab of fft2. Inverse: x is the column slab, y

@@ -131,3 +131,16 @@ def test_every_operator_schema_is_registered():
         assert hasattr(torch.ops.spectral, op), op
     schema = str(torch.ops.spectral.fft_c2c.default._schema)
     assert 'str impl="naive"' in schema and "bool inverse=False" in schema
+
+
+def test_slab_relayout_argument_checks():
+    import ctypes
+
+    table = (ctypes.c_void_p * 2)(8, 16)
+    with pytest.raises(ValueError, match="ranks must be from 1 to 16"):
+        native.call("spectral_slab_relayout", table, table, 17, 4, 4, 4, None)
+    with pytest.raises(ValueError, match="row strides of at least w"):
+        native.call("spectral_slab_relayout", table, table, 2, 4, 3, 4, None)
+    odd = (ctypes.c_void_p * 2)(8, 20)
+    with pytest.raises(ValueError, match="8-byte aligned"):
+        native.call("spectral_slab_relayout", odd, table, 2, 4, 4, 4, None)

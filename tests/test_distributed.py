@@ -1,5 +1,6 @@
 """The slab decomposition of the large 2D transform on CPU ranks (gloo): the chunk layout, the
-all-to-all and the column slab, with numpy stand-ins for the kernels (whose layouts the GPU
+all-to-all, the column slab and the natural-layout second exchange, with numpy stand-ins for the
+kernels (whose layouts the GPU
 tests in test_slab.py check). world_size 2 and 4, spawned processes."""
 
 import os
@@ -40,6 +41,15 @@ def columns_stub(x, n, width, inverse):
     return torch.from_numpy(y.astype(np.complex64))
 
 
+def relayout_stub(src, dst, ranks, w, src_offsets, src_stride, dst_offsets, dst_stride):
+    """The relayout kernel's contract on flat CPU tensors: block r, w rows of w values."""
+    s, d = src.reshape(-1), dst.reshape(-1)
+    for r in range(ranks):
+        for k in range(w):
+            a, b = src_offsets[r] + k * src_stride, dst_offsets[r] + k * dst_stride
+            d[b:b + w] = s[a:a + w]
+
+
 def worker(rank: int, world: int, port: int, out: dict) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -58,9 +68,20 @@ def worker(rank: int, world: int, port: int, out: dict) -> None:
         back = fft2_slab(cols, inverse=True, rows_fn=rows_stub, columns_fn=columns_stub)
         every = [torch.empty_like(back) for _ in range(world)]
         dist.all_gather(every, back)
+        # Natural layout: the second exchange returns the rank's rows of fft2, and the natural
+        # inverse takes them back to the rank's rows of the field.
+        stubs = dict(rows_fn=rows_stub, columns_fn=columns_stub, relayout_fn=relayout_stub)
+        nat = fft2_slab(x, layout="natural", **stubs)
+        nat_rows = [torch.empty_like(nat) for _ in range(world)]
+        dist.all_gather(nat_rows, nat)
+        nat_back = fft2_slab(nat, inverse=True, layout="natural", **stubs)
+        nat_every = [torch.empty_like(nat_back) for _ in range(world)]
+        dist.all_gather(nat_every, nat_back)
         if rank == 0:
             out["forward"] = torch.cat(gathered, dim=1).numpy()
             out["inverse"] = torch.cat(every, dim=0).numpy()
+            out["natural"] = torch.cat(nat_rows, dim=0).numpy()
+            out["natural_inverse"] = torch.cat(nat_every, dim=0).numpy()
     finally:
         dist.destroy_process_group()
 
@@ -73,3 +94,5 @@ def test_slab_decomposition_on_gloo_ranks(world):
     expected = np.fft.fft2(field().astype(np.complex128))
     np.testing.assert_allclose(out["forward"], expected, rtol=0, atol=1e-4 * np.abs(expected).max())
     np.testing.assert_allclose(out["inverse"], field(), rtol=0, atol=1e-5)
+    np.testing.assert_array_equal(out["natural"], out["forward"])
+    np.testing.assert_allclose(out["natural_inverse"], field(), rtol=0, atol=1e-5)

@@ -56,6 +56,24 @@ def _rank_main(rank: int, world: int, port: int, n: int) -> None:
             assert torch.equal(pback, back)
         plan.close()
 
+        # Natural layout: the rank's rows of fft2 by the second all-to-all and by peer memory,
+        # bit for bit the column slab's values, and back.
+        start = rank * w
+        expected_rows = np.fft.fft2(x.astype(np.complex128))[start:start + w]
+        nat = fft2_slab(local, layout="natural")
+        assert_transform_close(nat.cpu().numpy()[None], expected_rows[None], n * n, axes=(-2, -1))
+        nat_back = fft2_slab(nat, inverse=True, layout="natural")
+        assert_transform_close(nat_back.cpu().numpy()[None], x[rank * rows:(rank + 1) * rows][None],
+                               n * n, axes=(-2, -1), tol=2 * fft_tolerance(n * n))
+        gathered = [torch.empty_like(cols) for _ in range(world)]
+        dist.all_gather(gathered, cols)
+        assert torch.equal(nat, torch.cat(gathered, dim=1)[start:start + w])
+        nplan = PeerSlab(n, natural=True)
+        for _ in range(3):
+            assert torch.equal(nplan.forward_natural(local), nat)
+            assert torch.equal(nplan.inverse_natural(nat), nat_back)
+        nplan.close()
+
         # The same through the C ABI on an NCCL communicator of the library's own making.
         import ctypes
 

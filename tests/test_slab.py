@@ -72,3 +72,32 @@ def test_rejects_bad_shapes():
     x = torch.zeros(4, 12, dtype=torch.complex64, device="cuda")
     with pytest.raises(ValueError, match="power of two"):
         rows_kernel(x, 12, 4, 3, False)
+
+
+@pytest.mark.parametrize(("ranks", "w"), [(1, 8), (2, 512), (4, 1), (8, 3), (16, 64)])
+def test_relayout_moves_every_block(rng, ranks, w):
+    # Blocks of w x w between the two sides, both directions, odd and even w (the 16-byte and the
+    # 8-byte path), exact copies.
+    from spectral.distributed import relayout_kernel
+
+    n = ranks * w
+    blocks = torch.from_numpy((rng.standard_normal((ranks, w, w)) + 1j * rng.standard_normal((ranks, w, w)))
+                              .astype(np.complex64)).cuda()
+    rows = torch.empty((w, n), dtype=torch.complex64, device="cuda")
+    relayout_kernel(blocks, rows, ranks, w, [r * w * w for r in range(ranks)], w, [r * w for r in range(ranks)], n)
+    assert torch.equal(rows, blocks.permute(1, 0, 2).reshape(w, n))
+    back = torch.empty_like(blocks)
+    relayout_kernel(rows, back, ranks, w, [r * w for r in range(ranks)], n, [r * w * w for r in range(ranks)], w)
+    assert torch.equal(back, blocks)
+
+
+def test_natural_layout_on_one_rank_is_the_full_transform(rng):
+    from spectral.distributed import fft2_slab
+
+    n = 1024
+    x = (rng.standard_normal((n, n)) + 1j * rng.standard_normal((n, n))).astype(np.complex64)
+    y = fft2_slab(torch.from_numpy(x).cuda(), layout="natural")
+    assert y.shape == (n, n)
+    assert_transform_close(y.cpu().numpy()[None], np.fft.fft2(x.astype(np.complex128))[None], n * n, axes=(-2, -1))
+    back = fft2_slab(y, inverse=True, layout="natural")
+    assert_transform_close(back.cpu().numpy()[None], x[None], n * n, axes=(-2, -1), tol=2 * fft_tolerance(n * n))

@@ -4,8 +4,8 @@
 // shared memory, completed through an mbarrier, and the bounded waits on them.
 //
 // cp.async.bulk needs 16-byte aligned source and destination addresses and a size that is a
-// multiple of 16 bytes; callers check that on the host. The copies here never use
-// .multicast::cluster, and their sources are always this GPU's own memory.
+// multiple of 16 bytes; callers check that on the host. The copies here are never multicast to
+// other CTAs of a cluster, and their sources are always this GPU's own memory.
 //
 // Every wait is bounded: mbar_wait gives up after kSpinLimit polls (each poll already suspends
 // for a hardware-chosen time), and the kernel then records a fault code in a device word that

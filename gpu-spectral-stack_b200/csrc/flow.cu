@@ -105,22 +105,59 @@ struct ProductRowIo {
         field<PL>(v, c, 0);
     }
 
+    // The raw loads of field q's row (X[k] and X[M - k] of every element k the thread prepares),
+    // issued early so that they are in flight during the previous field's passes; finish() is
+    // C2rIo's prepare step on them.
+    template <class PL>
+    __device__ __forceinline__ void fetch(float2 (&a)[PL::E], float2 (&b)[PL::E], const RowCtx& c, int q) const
+    {
+        constexpr int N = PL::N;
+        const float2 zero = make_float2(0.0f, 0.0f);
+        const float2* row = y + (q * rows + c.tf) * m;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const int k = c.t + i * PL::P;
+            a[i] = (c.active && k < m) ? __ldg(row + k) : zero;
+            b[i] = (c.active && N - k < m) ? __ldg(row + (N - k)) : zero;
+        }
+    }
+
+    template <class PL>
+    __device__ __forceinline__ void finish(float2 (&v)[PL::E], float2 (&a)[PL::E], float2 (&b)[PL::E],
+                                           const RowCtx& c) const
+    {
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const int k = c.t + i * PL::P;
+            if (k == 0) {
+                a[i].y = 0.0f;
+                b[i].y = 0.0f;
+            }
+            v[i] = c2r_prepare(a[i], b[i], c.extra[k]);
+        }
+    }
+
     template <class PL, bool Inv>
     __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
     {
         // v = u as packed real pairs (x[2k], x[2k+1]); a product of real fields is the packed
-        // product of the pairs.
+        // product of the pairs. Each field's loads are issued before the previous field's passes.
         float2 acc[PL::E];
         float2 t[PL::E];
-        field<PL>(t, c, 2);
+        float2 a[PL::E];
+        float2 b[PL::E];
+        fetch<PL>(a, b, c, 2);
+        finish<PL>(t, a, b, c);
+        fetch<PL>(a, b, c, 1);
         run_passes<PL, true, B>(t, c.t, c.buf, tw);
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
             acc[i] = __fmul2_rn(v[i], t[i]);  // u wx
         }
-        field<PL>(v, c, 1);
+        finish<PL>(v, a, b, c);
+        fetch<PL>(a, b, c, 3);
         run_passes<PL, true, B>(v, c.t, c.buf, tw);
-        field<PL>(t, c, 3);
+        finish<PL>(t, a, b, c);
         run_passes<PL, true, B>(t, c.t, c.buf, tw);
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {

@@ -26,6 +26,7 @@
 
 #include "backend.hpp"
 #include "columns.cuh"
+#include "simple.cuh"
 
 #include <climits>
 #include <type_traits>
@@ -285,6 +286,49 @@ struct SlabColumnPass2Io {
     }
 };
 
+// The first stage of a 1D transform of n = n1 n2 points distributed over ranks (the four-step
+// algorithm, Bailey 1990): an (n1, width) row-major slab holds columns j2 = col0 .. col0+width-1
+// of the n1 x n2 view x[j1 n2 + j2]. Column c is an n1-point transform over j1; its output k1 is
+// multiplied by W_n^(k1 j2) (its conjugate for the inverse) and stored back at row k1 of y.
+struct SlabTwiddleColumnIo {
+    const float2* x;
+    float2* y;
+    int width;
+    long long col0;
+    long long n;
+    float scale;  // 1 / n1 for the inverse
+
+    template <class PL>
+    __device__ __forceinline__ void load(float2 (&v)[PL::E], const ColumnCtx& c) const
+    {
+        const float2* b = x + (c.active ? c.f : 0);
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            v[i] = c.active ? b[static_cast<long long>(c.t + i * PL::P) * width] : make_float2(0.0f, 0.0f);
+        }
+    }
+
+    template <class PL, int C, bool Inv>
+    __device__ __forceinline__ void store(float2 (&v)[PL::E], const ColumnCtx& c) const
+    {
+        if (!c.active) {
+            return;
+        }
+        const long long j2 = col0 + c.f;
+        const float step = 2.0f / static_cast<float>(n);  // exact: n is a power of two
+        float2* b = y + c.f;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            const long long k1 = c.t + i * PL::P;
+            float sn = 0.0f;
+            float cs = 1.0f;
+            sincospif(static_cast<float>(k1 * j2) * step, &sn, &cs);  // k1 j2 < n <= 2^24: exact
+            const float2 r = cmul_tw<Inv>(v[i], make_float2(cs, -sn));
+            b[k1 * width] = Inv ? cscale(r, scale) : r;
+        }
+    }
+};
+
 template <bool Inv>
 void slab_columns(float2* x, float2* y, int n, int w, cudaStream_t s)
 {
@@ -309,9 +353,9 @@ void slab_columns(float2* x, float2* y, int n, int w, cudaStream_t s)
 }
 
 // Block relayout between the column-slab side and the natural (row) side of the exchange: for
-// every rank r, the w x w block at src[r] (row stride src_stride) is copied to dst[r] (row stride
+// every rank r, the h x w block at src[r] (row stride src_stride) is copied to dst[r] (row stride
 // dst_stride). With the blocks' pointers chosen by the caller this is each of the four steps a
-// natural-layout transform needs:
+// natural-layout transform needs (square blocks, h = w, for the 2D slab):
 //   forward, received blocks -> rows:  src[r] = recv + r w^2 (w),  dst[r] = out + r w (n)
 //   inverse, rows -> send blocks:      src[r] = x + r w (n),       dst[r] = send + r w^2 (w)
 //   and the same with src[r] in another rank's memory (peer loads over NVLink, plain loads).
@@ -327,6 +371,7 @@ struct BlockTable {
 template <bool Pairs>
 __global__ void __launch_bounds__(256) slab_relayout_kernel(const BlockTable t, int w, long long src_stride,
                                                             long long dst_stride, long long per_rank)
+// per_rank = h * (vectors per block row); the row count itself is implied.
 {
     wait_for_previous_grid();
     allow_next_grid();
@@ -454,7 +499,60 @@ extern "C" int spectral_slab_rows_peer(const void* x, void* y, void* const* peer
     });
 }
 
-extern "C" int spectral_slab_relayout(const void* const* src, void* const* dst, int ranks, int w,
+extern "C" int spectral_slab_twiddle_columns(const void* x, void* y, int n1, int width, long long col0,
+                                             long long n, int inverse, void* stream)
+{
+    using namespace spectral;
+    return slab_guarded([&] {
+        if (!is_pow2(n1) || n1 < 2 || n1 > kMaxRowN) {
+            throw InvalidArgument("slab_twiddle_columns: n1 must be a power of two from 2 to "
+                                  + std::to_string(kMaxRowN) + ", got " + std::to_string(n1));
+        }
+        if (!is_pow2(n) || n % n1 != 0 || n > (1LL << 24)) {
+            throw InvalidArgument("slab_twiddle_columns: n must be a power of two multiple of n1, at most 2^24");
+        }
+        if (width < 1 || col0 < 0 || col0 + width > n / n1) {
+            throw InvalidArgument("slab_twiddle_columns: the slab's columns must lie in 0 .. n/n1 - 1");
+        }
+        if (x == y) {
+            throw InvalidArgument("slab_twiddle_columns: x and y must not overlap");
+        }
+        check_aligned(x);
+        check_aligned(y);
+        const auto s = static_cast<cudaStream_t>(stream);
+        dispatch_pow2<2, kMaxRowN>(n1, [&](auto n1_) {
+            constexpr int N1 = decltype(n1_)::value;
+            const SlabTwiddleColumnIo io{static_cast<const float2*>(x), static_cast<float2*>(y), width, col0, n,
+                                         1.0f / N1};
+            if (inverse) {
+                launch_columns<ColumnPlan<N1>, true, 8, false>(io, width, s);
+            } else {
+                launch_columns<ColumnPlan<N1>, false, 8, false>(io, width, s);
+            }
+        });
+    });
+}
+
+extern "C" int spectral_transpose(const void* x, void* y, int rows, int cols, long long batch, void* stream)
+{
+    using namespace spectral;
+    return slab_guarded([&] {
+        if (rows < 1 || cols < 1 || batch < 0) {
+            throw InvalidArgument("transpose: need rows, cols >= 1 and batch >= 0");
+        }
+        if (x == y) {
+            throw InvalidArgument("transpose: x and y must not overlap");
+        }
+        check_aligned(x);
+        check_aligned(y);
+        if (batch > 0) {
+            simple::transpose(static_cast<const float2*>(x), static_cast<float2*>(y), rows, cols, batch,
+                              static_cast<cudaStream_t>(stream));
+        }
+    });
+}
+
+extern "C" int spectral_slab_relayout(const void* const* src, void* const* dst, int ranks, int h, int w,
                                       long long src_stride, long long dst_stride, void* stream)
 {
     using namespace spectral;
@@ -462,8 +560,8 @@ extern "C" int spectral_slab_relayout(const void* const* src, void* const* dst, 
         if (ranks < 1 || ranks > kMaxRelayoutRanks) {
             throw InvalidArgument("slab_relayout: ranks must be from 1 to " + std::to_string(kMaxRelayoutRanks));
         }
-        if (w < 1 || src_stride < w || dst_stride < w) {
-            throw InvalidArgument("slab_relayout: need w >= 1 and row strides of at least w");
+        if (h < 1 || w < 1 || src_stride < w || dst_stride < w) {
+            throw InvalidArgument("slab_relayout: need h, w >= 1 and row strides of at least w");
         }
         if (src == nullptr || dst == nullptr) {
             throw InvalidArgument("slab_relayout: src and dst must list one block per rank");
@@ -481,7 +579,7 @@ extern "C" int spectral_slab_relayout(const void* const* src, void* const* dst, 
             t.src[r] = static_cast<const float2*>(src[r]);
             t.dst[r] = static_cast<float2*>(dst[r]);
         }
-        const long long per_rank = static_cast<long long>(w) * (pairs ? w / 2 : w);
+        const long long per_rank = static_cast<long long>(h) * (pairs ? w / 2 : w);
         const long long blocks_x = (per_rank + 255) / 256;
         const dim3 grid(static_cast<unsigned>(blocks_x < 4096 ? blocks_x : 4096), static_cast<unsigned>(ranks));
         const auto s = static_cast<cudaStream_t>(stream);

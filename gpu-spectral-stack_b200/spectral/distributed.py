@@ -55,13 +55,15 @@ def columns_kernel(x: torch.Tensor, n: int, width: int, inverse: bool) -> torch.
 
 
 def relayout_kernel(src: torch.Tensor, dst: torch.Tensor, ranks: int, w: int, src_offsets, src_stride: int,
-                    dst_offsets, dst_stride: int) -> None:
-    """Copies, for each rank r, the w x w block of src at element offset src_offsets[r] (row stride
-    src_stride) to dst at dst_offsets[r] (row stride dst_stride), complex64 on one device."""
+                    dst_offsets, dst_stride: int, h: int | None = None) -> None:
+    """Copies, for each rank r, the h x w block (h = w unless given) of src at element offset
+    src_offsets[r] (row stride src_stride) to dst at dst_offsets[r] (row stride dst_stride),
+    complex64 on one device."""
     table = ctypes.c_void_p * ranks
     sp = table(*[src.data_ptr() + 8 * o for o in src_offsets])
     dp = table(*[dst.data_ptr() + 8 * o for o in dst_offsets])
-    native.call("spectral_slab_relayout", sp, dp, ranks, w, src_stride, dst_stride, _stream())
+    native.call("spectral_slab_relayout", sp, dp, ranks, w if h is None else h, w, src_stride, dst_stride,
+                _stream())
 
 
 def _blocks_to_rows(recv: torch.Tensor, ranks: int, w: int, relayout_fn) -> torch.Tensor:
@@ -138,6 +140,81 @@ def fft2_slab(
     cols = columns_fn(x.contiguous().clone(), n, w, True)                # (n, w) = (ranks, rows, w)
     received = _exchange(cols.reshape(ranks, n // ranks, w), group)
     return rows_fn(received, n, n // ranks, ranks, True)
+
+
+# --- the 1D transform of one long signal, distributed by contiguous chunks --------------------
+
+
+def twiddle_columns_kernel(x: torch.Tensor, n1: int, width: int, col0: int, n: int, inverse: bool) -> torch.Tensor:
+    """n1-point transforms down the columns of an (n1, width) slab holding columns col0 .. of the
+    n1 x (n / n1) view of a signal, output k1 of column j2 times W_n^(k1 j2) (conjugate and / n1
+    for the inverse)."""
+    y = torch.empty((n1, width), dtype=torch.complex64, device=x.device)
+    native.call("spectral_slab_twiddle_columns", x.data_ptr(), y.data_ptr(), n1, width, col0, n,
+                1 if inverse else 0, _stream())
+    return y
+
+
+def c2c_rows_kernel(x: torch.Tensor, n2: int, inverse: bool) -> torch.Tensor:
+    """n2-point transforms of the rows of x (inverse divided by n2)."""
+    y = torch.empty_like(x)
+    native.call("spectral_c2c", b"stockham_r8", x.data_ptr(), y.data_ptr(), n2, x.numel() // n2,
+                1 if inverse else 0, _stream())
+    return y
+
+
+def transpose_kernel(x: torch.Tensor) -> torch.Tensor:
+    rows, cols = x.shape
+    y = torch.empty((cols, rows), dtype=torch.complex64, device=x.device)
+    native.call("spectral_transpose", x.data_ptr(), y.data_ptr(), rows, cols, 1, _stream())
+    return y
+
+
+def fft_slab(
+    x: torch.Tensor,
+    *,
+    inverse: bool = False,
+    group=None,
+    relayout_fn: Callable = relayout_kernel,
+    twiddle_fn: Callable = twiddle_columns_kernel,
+    rows_fn: Callable = c2c_rows_kernel,
+    transpose_fn: Callable = transpose_kernel,
+) -> torch.Tensor:
+    """The 1D FFT (or inverse FFT, divided by n) of one complex64 signal of n = R * len(x) points
+    (a power of two up to 2^24) held by the R ranks of the group in contiguous chunks: rank r holds
+    x[r n/R .. (r+1) n/R) and receives the same chunk of the transform.
+
+    The four-step algorithm over the n1 x n2 view (n1 = 2^floor(log2(n) / 2)): the column
+    transforms with the inter-step twiddles on each rank's column slab, the row transforms on its
+    rows, and three all-to-alls between those layouts (in, between, out); the relayout and a
+    transpose fit the blocks together (spectral_slab_twiddle_columns, spectral_c2c,
+    spectral_slab_relayout, spectral_transpose)."""
+    ranks, rank = _world(group)
+    if x.dtype != torch.complex64 or x.dim() != 1:
+        raise ValueError("fft_slab: x must be a 1D complex64 tensor (this rank's chunk)")
+    n = x.numel() * ranks
+    if n < 4 or n & (n - 1) or n > 1 << 24:
+        raise ValueError(f"fft_slab: the signal's length must be a power of two from 4 to 2^24, got {n}")
+    n1 = 1 << ((n.bit_length() - 1) // 2)
+    n2 = n // n1
+    if n1 % ranks:
+        raise ValueError(f"fft_slab: {ranks} ranks do not divide the {n1} x {n2} view of {n} points")
+    h1, w2 = n1 // ranks, n2 // ranks
+    blocks = [r * h1 * w2 for r in range(ranks)]
+
+    def rows_to_blocks(a: torch.Tensor) -> torch.Tensor:
+        send = torch.empty((ranks, h1, w2), dtype=torch.complex64, device=a.device)
+        relayout_fn(a, send, ranks, w2, [r * w2 for r in range(ranks)], n2, blocks, w2, h=h1)
+        return send
+
+    recv = _exchange(rows_to_blocks(x.contiguous().reshape(h1, n2)), group)            # (n1, w2) column slab
+    y = twiddle_fn(recv.reshape(n1, w2), n1, w2, rank * w2, n, inverse)
+    back = _exchange(y.reshape(ranks, h1, w2), group)                                  # my rows, by column block
+    rows = torch.empty((h1, n2), dtype=torch.complex64, device=x.device)
+    relayout_fn(back, rows, ranks, w2, blocks, w2, [r * w2 for r in range(ranks)], n2, h=h1)
+    z = rows_fn(rows, n2, inverse)
+    out = _exchange(rows_to_blocks(z), group)                                         # (n1, w2): Z[k1][k2 mine]
+    return transpose_fn(out.reshape(n1, w2)).reshape(-1)
 
 
 class PeerSlab:
@@ -246,7 +323,7 @@ class PeerSlab:
         w = self.w
         src = (ctypes.c_void_p * self.ranks)(*[slabs[r] + 8 * self.rank * w * w for r in range(self.ranks)])
         dst = (ctypes.c_void_p * self.ranks)(*[out.data_ptr() + 8 * r * w for r in range(self.ranks)])
-        native.call("spectral_slab_relayout", src, dst, self.ranks, w, w, self.n, _stream())
+        native.call("spectral_slab_relayout", src, dst, self.ranks, w, w, w, self.n, _stream())
         return out
 
     def inverse_natural(self, x: torch.Tensor) -> torch.Tensor:
@@ -264,7 +341,7 @@ class PeerSlab:
         cols = torch.empty((self.n, w), dtype=torch.complex64, device=x.device)
         src = (ctypes.c_void_p * self.ranks)(*[staged[r] + 8 * self.rank * w for r in range(self.ranks)])
         dst = (ctypes.c_void_p * self.ranks)(*[cols.data_ptr() + 8 * r * w * w for r in range(self.ranks)])
-        native.call("spectral_slab_relayout", src, dst, self.ranks, w, self.n, w, _stream())
+        native.call("spectral_slab_relayout", src, dst, self.ranks, w, w, self.n, w, _stream())
         return self._inverse(cols, b)
 
     def inverse(self, cols: torch.Tensor) -> torch.Tensor:

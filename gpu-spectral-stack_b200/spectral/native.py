@@ -61,7 +61,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_slab_rows": (_i, [_p, _p, _i, _ll, _i, _i, _p]),
     "spectral_slab_columns": (_i, [_p, _p, _i, _i, _i, _p]),
     "spectral_slab_rows_peer": (_i, [_p, _p, ctypes.POINTER(_p), _i, _ll, _i, _i, _i, _p]),
-    "spectral_slab_relayout": (_i, [ctypes.POINTER(_p), ctypes.POINTER(_p), _i, _i, _ll, _ll, _p]),
+    "spectral_slab_relayout": (_i, [ctypes.POINTER(_p), ctypes.POINTER(_p), _i, _i, _i, _ll, _ll, _p]),
+    "spectral_slab_twiddle_columns": (_i, [_p, _p, _i, _i, _ll, _ll, _i, _p]),
+    "spectral_transpose": (_i, [_p, _p, _i, _i, _ll, _p]),
     "spectral_fft2_slab_workspace": (_i, [_i, _i, _szp]),
     "spectral_fft2_slab": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),
     "spectral_slab_exchange": (_i, [_p, _p, _ll, _i, _p, _p]),

@@ -186,14 +186,31 @@ SPECTRAL_API int spectral_slab_rows_peer(const void* x, void* y, void* const* pe
 
 /* Natural layout. The column slab leaves rank r with output columns [r w, (r+1) w); a second
  * exchange of its w x w row blocks returns rows [r w, (r+1) w) of the transform instead. This
- * entry point copies, for each rank r (at most 16), the w x w block at src[r] (row stride
- * src_stride complex values) to dst[r] (row stride dst_stride). After the exchange of the column
+ * entry point copies, for each rank r (at most 16), the h x w block at src[r] (row stride
+ * src_stride complex values) to dst[r] (row stride dst_stride); the 2D slab uses h = w. After the exchange of the column
  * slab's row blocks, src[r] = recv + r w^2 (stride w) and dst[r] = out + r w (stride n) give
  * the natural w x n rows. Before an inverse, src[r] = x + r w (stride n) and dst[r] = send +
  * r w^2 (stride w) pack the send blocks. src[r] may be another rank's buffer mapped through
  * CUDA IPC (plain NVLink loads), which fuses the exchange into the copy. */
-SPECTRAL_API int spectral_slab_relayout(const void* const* src, void* const* dst, int ranks, int w,
+SPECTRAL_API int spectral_slab_relayout(const void* const* src, void* const* dst, int ranks, int h, int w,
                                         long long src_stride, long long dst_stride, void* stream);
+
+/* The 1D transform of n = n1 n2 points (n at most 2^24) distributed over ranks, each holding a
+ * contiguous n / ranks of the signal (no counterpart in the reference, which has no multi-GPU
+ * code). Viewing x as n1 rows by n2 columns, x[j1 n2 + j2]:
+ *   1. the relayout packs the rank's rows into blocks of n1/R x n2/R; an all-to-all gives each rank
+ *      the (n1, n2/R) slab of its columns j2 = col0 .. col0 + n2/R - 1;
+ *   2. spectral_slab_twiddle_columns: n1-point transforms down that slab, output k1 multiplied by
+ *      W_n^(k1 j2) (conjugate for the inverse, which also divides by n1);
+ *   3. an all-to-all of the slab's row blocks and the relayout give the rank's n1/R rows k1;
+ *   4. spectral_c2c: n2-point row transforms;
+ *   5. the relayout packs the row blocks; an all-to-all gives each rank the (n1, n2/R) slab of
+ *      its columns k2; spectral_transpose turns it into (n2/R, n1): X[k1 + n1 k2] for the rank's
+ *      k2, its contiguous share of the output.
+ * spectral_transpose: y = the transpose of `batch` row-major rows x cols arrays. */
+SPECTRAL_API int spectral_slab_twiddle_columns(const void* x, void* y, int n1, int width, long long col0,
+                                               long long n, int inverse, void* stream);
+SPECTRAL_API int spectral_transpose(const void* x, void* y, int rows, int cols, long long batch, void* stream);
 
 /* The whole slab transform through the C ABI, with the exchange on an NCCL communicator given as
  * void* (ncclComm_t; no counterpart in the reference). Forward: x is this rank's n/ranks rows

@@ -138,9 +138,13 @@ def test_slab_relayout_argument_checks():
 
     table = (ctypes.c_void_p * 2)(8, 16)
     with pytest.raises(ValueError, match="ranks must be from 1 to 16"):
-        native.call("spectral_slab_relayout", table, table, 17, 4, 4, 4, None)
+        native.call("spectral_slab_relayout", table, table, 17, 4, 4, 4, 4, None)
     with pytest.raises(ValueError, match="row strides of at least w"):
-        native.call("spectral_slab_relayout", table, table, 2, 4, 3, 4, None)
+        native.call("spectral_slab_relayout", table, table, 2, 4, 4, 3, 4, None)
     odd = (ctypes.c_void_p * 2)(8, 20)
     with pytest.raises(ValueError, match="8-byte aligned"):
-        native.call("spectral_slab_relayout", odd, table, 2, 4, 4, 4, None)
+        native.call("spectral_slab_relayout", odd, table, 2, 4, 4, 4, 4, None)
+    with pytest.raises(ValueError, match="columns must lie in"):
+        native.call("spectral_slab_twiddle_columns", 8, 16, 64, 8, 60, 4096, 0, None)
+    with pytest.raises(ValueError, match="must not overlap"):
+        native.call("spectral_transpose", 8, 8, 4, 4, 1, None)

@@ -111,3 +111,39 @@ def test_slab_across_two_gpus(n):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     torch.multiprocessing.spawn(_rank_main, args=(2, _free_port(), n), nprocs=2, join=True)
+
+
+def _rank_main_1d(rank: int, world: int, port: int, n: int) -> None:
+    import torch.distributed as dist
+
+    from oracle.policy import assert_transform_close, fft_tolerance
+    from spectral.distributed import fft_slab
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        rng = np.random.default_rng(8)
+        x = (rng.standard_normal(n) + 1j * rng.standard_normal(n)).astype(np.complex64)
+        chunk = n // world
+        mine = slice(rank * chunk, (rank + 1) * chunk)
+        y = fft_slab(torch.from_numpy(x[mine]).cuda())
+        expected = np.fft.fft(x.astype(np.complex128))
+        # This rank's chunk of one n-point transform, against the bound for the whole transform.
+        scale = np.linalg.norm(expected) / np.sqrt(world)
+        err = np.linalg.norm(y.cpu().numpy() - expected[mine]) / scale
+        assert err <= fft_tolerance(n), err
+        back = fft_slab(y, inverse=True)
+        assert_transform_close(back.cpu().numpy()[None], x[mine][None], n, tol=2 * fft_tolerance(n))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n", [1 << 16, 1 << 24])
+def test_distributed_1d_transform_across_two_gpus(n):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    torch.multiprocessing.spawn(_rank_main_1d, args=(2, _free_port(), n), nprocs=2, join=True)

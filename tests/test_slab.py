@@ -101,3 +101,41 @@ def test_natural_layout_on_one_rank_is_the_full_transform(rng):
     assert_transform_close(y.cpu().numpy()[None], np.fft.fft2(x.astype(np.complex128))[None], n * n, axes=(-2, -1))
     back = fft2_slab(y, inverse=True, layout="natural")
     assert_transform_close(back.cpu().numpy()[None], x[None], n * n, axes=(-2, -1), tol=2 * fft_tolerance(n * n))
+
+
+# --- the distributed 1D transform's kernels -------------------------------------------------------
+
+
+@pytest.mark.parametrize(("n1", "width", "col0", "n"), [(64, 16, 48, 4096), (4096, 8, 4088, 1 << 24), (2, 1, 1, 4)])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_twiddle_columns_match_the_oracle(rng, n1, width, col0, n, inverse):
+    from spectral.distributed import twiddle_columns_kernel
+
+    x = (rng.standard_normal((n1, width)) + 1j * rng.standard_normal((n1, width))).astype(np.complex64)
+    y = twiddle_columns_kernel(torch.from_numpy(x).cuda(), n1, width, col0, n, inverse).cpu().numpy()
+    a = x.astype(np.complex128)
+    ref = np.fft.ifft(a, axis=0) if inverse else np.fft.fft(a, axis=0)
+    k1 = np.arange(n1)[:, None]
+    j2 = (col0 + np.arange(width))[None, :]
+    ref = ref * np.exp((2j if inverse else -2j) * np.pi * ((k1 * j2) % n) / n)
+    assert_transform_close(y.T, ref.T, n1, tol=2 * fft_tolerance(n1))
+
+
+def test_transpose_entry_point(rng):
+    from spectral.distributed import transpose_kernel
+
+    x = torch.from_numpy((rng.standard_normal((96, 40)) + 1j * rng.standard_normal((96, 40))).astype(np.complex64)).cuda()
+    assert torch.equal(transpose_kernel(x), x.t().contiguous())
+
+
+@pytest.mark.parametrize("n", [16, 1 << 12, 1 << 17, 1 << 24])
+def test_distributed_1d_transform_on_one_rank(rng, n):
+    # One rank: the four-step path of fft_slab (twiddled columns, rows, transpose) against the
+    # oracle, and back.
+    from spectral.distributed import fft_slab
+
+    x = (rng.standard_normal(n) + 1j * rng.standard_normal(n)).astype(np.complex64)
+    y = fft_slab(torch.from_numpy(x).cuda())
+    assert_transform_close(y.cpu().numpy()[None], np.fft.fft(x.astype(np.complex128))[None], n)
+    back = fft_slab(y, inverse=True)
+    assert_transform_close(back.cpu().numpy()[None], x[None], n, tol=2 * fft_tolerance(n))

@@ -1,7 +1,7 @@
 """Benchmark of the batched-FFT hot path: one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload real|c2c|rfft2|pruned|slab|spectrum|fir|flow] [--fft-impl stockham_r8]
+                    [--workload real|c2c|rfft2|pruned|slab|spectrum|fir|flow|fft1d] [--fft-impl stockham_r8]
 
 The headline workload is the one the metric is quoted on (configs[1] of BASELINE.json): a step
 is rfft then irfft of 4096 rows of 4096 float32 samples, iid U[-1, 1] from a seed, 2^24 points
@@ -59,7 +59,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=500)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["real", "c2c", "rfft2", "pruned", "slab", "spectrum", "fir", "flow"],
+    p.add_argument("--workload", choices=["real", "c2c", "rfft2", "pruned", "slab", "spectrum", "fir", "flow",
+                                          "fft1d"],
                    default="real")
     p.add_argument("--fft-impl", default="stockham_r8", help="registry name (spectral.FFT_IMPLS)")
     p.add_argument("--columns", default="strided", help="rfft2 workload: strided or transpose")
@@ -746,6 +747,72 @@ def run_flow_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_fft1d(args) -> None:
+    """One 2^24-point complex signal held by the ranks in contiguous chunks, transformed by
+    spectral.distributed.fft_slab (four-step over the ranks, three all-to-alls): strong scaling.
+    Bytes: 16 per point of the signal (the reference's convention), 256 MiB per transform."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    from spectral.distributed import fft_slab
+
+    n = 1 << 24
+    chunk = n // world
+    g = torch.Generator(device="cuda").manual_seed(6000 + rank)
+    xs = [torch.complex(torch.randn(chunk, device="cuda", generator=g), torch.randn(chunk, device="cuda", generator=g))
+          for _ in range(2)]
+    stream = torch.cuda.current_stream()
+    for k in range(args.warmup):
+        fft_slab(xs[k % 2])
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for k in range(args.steps):
+            fft_slab(xs[k % 2])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(stop)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    max_ms = float(t.item())
+    peak, peak_source = hbm_peak()
+    value = 16 * n * args.steps / (max_ms * 1e-3) / 1e9
+    # Bound: about six passes over the rank's chunk (pack, columns, unpack, rows, pack, transpose),
+    # each reading and writing it, against three exchanges of (R-1)/R of it over NVLink.
+    chunk_bytes = 8 * n / world
+    hbm_s = 6 * 2 * chunk_bytes / (peak * 1e9)
+    link_s = 3 * chunk_bytes * (world - 1) / world / 770e9
+    bound_s = max(hbm_s, link_s)
+    step_s = max_ms / args.steps * 1e-3
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "1D c64 transform of one 2^24-point signal in contiguous chunks over the ranks "
+                               "(spectral.distributed.fft_slab)", "ranks": world},
+        "roofline": {"bound": "hbm" if hbm_s >= link_s else "nvlink", "achieved_s": round(step_s, 6),
+                     "bound_s": round(bound_s, 6), "frac": round(bound_s / step_s, 4),
+                     "peak_source": f"{peak_source} HBM {peak} GB/s; NVLink 770 GB/s per direction (measured)"},
+        "cpu_baseline": None, "e2e": None, "gpu_launches": None, "clocks": clocks.summary(), "impl": "ours",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def make_workload(args):
     if args.workload == "real":
         return Real(args.fft_impl)
@@ -759,6 +826,10 @@ def make_workload(args):
         return Spectrum(args.fft_impl)
     if args.workload == "fir":
         return Fir(args.fft_impl)
+    if args.workload == "fft1d":  # the reference arm: one 2^24-point transform and its inverse
+        wl = C2c(args.fft_impl, batch=1, n=1 << 24)
+        wl.name = "fft_c2c fwd+inv of one 2^24-point c64 signal"
+        return wl
     return Pruned(args.fft_impl)
 
 
@@ -1090,6 +1161,8 @@ def main() -> None:
     args = parse()
     if args.workload == "flow":
         (run_flow_reference if args.impl == "reference" else run_flow)(args)
+    elif args.workload == "fft1d" and args.impl == "ours":
+        run_fft1d(args)
     elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "slab":

@@ -100,6 +100,15 @@ struct OverlapSaveIo {
         const long long r = c.tf / blocks;
         const long long start = (c.tf - r * blocks) * (PL::N - m + 1) - (m - 1);
         const float2* row = x + r * n;
+        if (c.active && start >= 0 && start + PL::N <= n) {
+            // Interior block (every block but the first and the last of a row): no bounds.
+            const float2* p = row + start + c.t;
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = __ldg(p + i * PL::P);
+            }
+            return;
+        }
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
             const long long p = start + c.t + i * PL::P;
@@ -124,14 +133,25 @@ struct OverlapSaveIo {
         const long long r = c.tf / blocks;
         const long long b = c.tf - r * blocks;
         const int L = PL::N - m + 1;
-        float2* row = y + r * n;
         constexpr float kScale = 1.0f / PL::N;
+        // Output k >= m - 1 of the block is sample b L + k - (m - 1) of the row.
+        float2* out = y + r * n + b * L;
+        if (b * L + L <= n) {  // every output of the block lies inside the row
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                const int k = c.t + i * PL::P;
+                if (k >= m - 1) {
+                    out[k - (m - 1)] = cscale(v[i], kScale);
+                }
+            }
+            return;
+        }
+        const int last = static_cast<int>(n - b * L) + (m - 1);  // outputs k < last lie in the row
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
             const int k = c.t + i * PL::P;
-            const long long p = b * L + (k - (m - 1));
-            if (k >= m - 1 && p < n) {
-                row[p] = cscale(v[i], kScale);
+            if (k >= m - 1 && k < last) {
+                out[k - (m - 1)] = cscale(v[i], kScale);
             }
         }
     }

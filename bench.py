@@ -578,7 +578,6 @@ def run_flow(args) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    import spectral
     from spectral.flow import Flow
     from spectral.flow.gpu import GpuSolver
 

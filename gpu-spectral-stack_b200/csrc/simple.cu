@@ -31,34 +31,61 @@ __global__ void scale_kernel(const float2* __restrict__ x, float2* __restrict__ 
     }
 }
 
-// 32 x 32 tiles through shared memory, one extra column so a warp's column reads of the tile
-// fall in different banks. Reads and writes are both whole rows of 32 values.
-constexpr int kTile = 32;
+// 64 x 64 tiles through shared memory, one extra column so that a warp's column reads of the
+// tile spread over the banks. A CTA of 32 x 8 threads moves a tile with 16 loads per thread, all
+// issued before the first store, and walks the tiles of the batch with a grid stride. Reads and
+// writes are runs of 32 consecutive values (256 bytes) per warp.
+constexpr int kTile = 64;
 constexpr int kTileRows = 8;
 
-__global__ void transpose_kernel(const float2* __restrict__ x, float2* __restrict__ y, int rows,
-                                 int cols, long long batch)
+__global__ void __launch_bounds__(32 * kTileRows)
+    transpose_kernel(const float2* __restrict__ x, float2* __restrict__ y, int rows, int cols, long long batch)
 {
     wait_for_previous_grid();
     allow_next_grid();
     __shared__ float2 tile[kTile][kTile + 1];
     const long long size = static_cast<long long>(rows) * cols;
-    for (long long b = blockIdx.z; b < batch; b += gridDim.z) {
+    const int tiles_x = (cols + kTile - 1) / kTile;
+    const int tiles_y = (rows + kTile - 1) / kTile;
+    const long long per = static_cast<long long>(tiles_x) * tiles_y;
+    const int tx = threadIdx.x;
+    const int ty = threadIdx.y;
+    for (long long g = blockIdx.x; g < per * batch; g += gridDim.x) {
+        const long long b = g / per;
+        const int t = static_cast<int>(g - b * per);
+        const int r0 = (t / tiles_x) * kTile;
+        const int c0 = (t - (t / tiles_x) * tiles_x) * kTile;
         const float2* xs = x + b * size;
         float2* ys = y + b * size;
-        const int c = blockIdx.x * kTile + threadIdx.x;
-        for (int k = threadIdx.y; k < kTile; k += kTileRows) {
-            const int r = blockIdx.y * kTile + k;
-            if (r < rows && c < cols) {
-                tile[k][threadIdx.x] = xs[static_cast<long long>(r) * cols + c];
+        float2 v[2][kTile / kTileRows];
+#pragma unroll
+        for (int k = 0; k < kTile / kTileRows; ++k) {
+            const int r = r0 + ty + k * kTileRows;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int c = c0 + tx + 32 * h;
+                v[h][k] = (r < rows && c < cols) ? xs[static_cast<long long>(r) * cols + c] : make_float2(0.0f, 0.0f);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kTile / kTileRows; ++k) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                tile[ty + k * kTileRows][tx + 32 * h] = v[h][k];
             }
         }
         __syncthreads();
-        const int r_out = blockIdx.y * kTile + threadIdx.x;
-        for (int k = threadIdx.y; k < kTile; k += kTileRows) {
-            const int c_out = blockIdx.x * kTile + k;
-            if (r_out < rows && c_out < cols) {
-                ys[static_cast<long long>(c_out) * rows + r_out] = tile[threadIdx.x][k];
+        // Output row c0 + j holds input column c0 + j; its values are the tile's column j.
+#pragma unroll
+        for (int k = 0; k < kTile / kTileRows; ++k) {
+            const int j = ty + k * kTileRows;
+            const int c_out = c0 + j;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r_out = r0 + tx + 32 * h;
+                if (c_out < cols && r_out < rows) {
+                    ys[static_cast<long long>(c_out) * rows + r_out] = tile[tx + 32 * h][j];
+                }
             }
         }
         __syncthreads();
@@ -193,10 +220,10 @@ void transpose(const float2* x, float2* y, int rows, int cols, long long batch, 
     if (batch <= 0 || rows <= 0 || cols <= 0) {
         return;
     }
-    const dim3 block(kTile, kTileRows);
-    const dim3 grid(static_cast<unsigned>((cols + kTile - 1) / kTile),
-                    static_cast<unsigned>((rows + kTile - 1) / kTile),
-                    static_cast<unsigned>(std::min(batch, 65535LL)));
+    const dim3 block(32, kTileRows);
+    const long long tiles = static_cast<long long>((cols + kTile - 1) / kTile) * ((rows + kTile - 1) / kTile) * batch;
+    const long long cap = static_cast<long long>(device_sm_count(current_device())) * 6;  // resident: 6 CTAs of 33 KB per SM
+    const dim3 grid(static_cast<unsigned>(std::min(tiles, cap)));
     launch_pdl(transpose_kernel, grid, block, 0, s, x, y, rows, cols, batch);
 }
 

@@ -60,9 +60,27 @@ struct SlabRowIo {
         return ((static_cast<long long>(s) * rows + row) << wlog) + (k & ((1 << wlog) - 1));
     }
 
+    // Where chunks are whole multiples of the plan's P threads (w >= P), element t + i P of a
+    // row lies in chunk (i P) >> wlog at offset t + ((i P) & (w - 1)): one base address per row,
+    // a chunk stride and compile-time offsets instead of the index arithmetic per element.
+    template <class PL>
+    __device__ __forceinline__ long long chunked_fast(int i) const
+    {
+        const int off = i * PL::P;
+        return static_cast<long long>(off >> wlog) * (rows << wlog) + (off & ((1 << wlog) - 1));
+    }
+
     template <class PL>
     __device__ __forceinline__ void load(float2 (&v)[PL::E], long long row, int t) const
     {
+        if (Inv && (1 << wlog) >= PL::P) {
+            const float2* b = x + (row << wlog) + t;
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = b[chunked_fast<PL>(i)];
+            }
+            return;
+        }
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
             const int k = t + i * PL::P;
@@ -73,6 +91,14 @@ struct SlabRowIo {
     template <class PL>
     __device__ __forceinline__ void store(float2 (&v)[PL::E], long long row, int t) const
     {
+        if (!Inv && (1 << wlog) >= PL::P) {
+            float2* b = y + (row << wlog) + t;
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                b[chunked_fast<PL>(i)] = v[i];
+            }
+            return;
+        }
 #pragma unroll
         for (int i = 0; i < PL::E; ++i) {
             const int k = t + i * PL::P;

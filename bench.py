@@ -700,7 +700,8 @@ def run_flow(args) -> None:
                    "back_to_back_trajectory_steps_per_s": round(world * batch * args.steps / (b2b_ms * 1e-3), 1),
                    "published_baseline": "108,682 trajectory-steps/s, stockham_r8 pruned, RTX 5080 Laptop GPU"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": None, "clocks": clocks.summary(), "impl": "ours",
+        # Per step: two stages of three fused kernels (the composed path is not counted).
+        "gpu_launches": args.steps * 6 if solver.fused else None, "clocks": clocks.summary(), "impl": "ours",
     }
     print(json.dumps(line), flush=True)
 
@@ -807,7 +808,9 @@ def run_fft1d(args) -> None:
         "roofline": {"bound": "hbm" if hbm_s >= link_s else "nvlink", "achieved_s": round(step_s, 6),
                      "bound_s": round(bound_s, 6), "frac": round(bound_s / step_s, 4),
                      "peak_source": f"{peak_source} HBM {peak} GB/s; NVLink 770 GB/s per direction (measured)"},
-        "cpu_baseline": None, "e2e": None, "gpu_launches": None, "clocks": clocks.summary(), "impl": "ours",
+        # Per transform: relayout, twiddled columns, relayout, rows, relayout, transpose (the
+        # all-to-alls are NCCL's).
+        "cpu_baseline": None, "e2e": None, "gpu_launches": args.steps * 6, "clocks": clocks.summary(), "impl": "ours",
     }
     print(json.dumps(line), flush=True)
 

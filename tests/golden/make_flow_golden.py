@@ -1,6 +1,6 @@
 """Generates tests/golden/flow_golden.npz from the REFERENCE's own float64 Navier-Stokes solver.
 
-    python tests/golden/make_flow_golden.py [path/to/gpu-spectral-stack]
+    python tests/golden/make_flow_golden.py path/to/gpu-spectral-stack
 
 Loads python/spectral/flow/params.py and reference.py of the reference checkout by file path
 under a stand-in package (they need only numpy) and records, for seeded initial conditions:
@@ -83,4 +83,6 @@ def main(root: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {Path(__file__).name} path/to/gpu-spectral-stack")
+    main(Path(sys.argv[1]))

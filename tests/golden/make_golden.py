@@ -1,6 +1,6 @@
 """Generates tests/golden/reference_golden.npz from the REFERENCE's own float64 oracle.
 
-    python tests/golden/make_golden.py [path/to/gpu-spectral-stack]
+    python tests/golden/make_golden.py path/to/gpu-spectral-stack
 
 Imports python/spectral/reference.py of the reference checkout by file path (it needs only
 numpy; the package's __init__ would need its CUDA extension) and records, for small seeded
@@ -88,4 +88,6 @@ def main(root: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {Path(__file__).name} path/to/gpu-spectral-stack")
+    main(Path(sys.argv[1]))

@@ -1,6 +1,6 @@
 """Generates tests/golden/rf_golden.npz from the REFERENCE's own python/spectral/rf.py.
 
-    python tests/golden/make_rf_golden.py [path/to/gpu-spectral-stack]
+    python tests/golden/make_rf_golden.py path/to/gpu-spectral-stack
 
 rf.py imports its package's `ops` (which needs the reference's CUDA extension) only for the
 names of its FFT implementations, so it is loaded by file path under a stand-in package whose
@@ -86,4 +86,6 @@ def main(root: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {Path(__file__).name} path/to/gpu-spectral-stack")
+    main(Path(sys.argv[1]))

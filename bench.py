@@ -968,7 +968,7 @@ def cpu_sample_rows(wl) -> int:
         return 4
     if isinstance(wl, Rfft2):
         return 64
-    return 1024
+    return min(1024, getattr(wl, "batch", 1024))  # never more rows than the workload has
 
 
 def run_reference(args) -> None:

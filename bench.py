@@ -992,7 +992,8 @@ def run_reference(args) -> None:
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1000 * t, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(1000 * t, 3), "higher_is_better": True,
+        "scaling": "strong" if args.workload in ("slab", "fft1d") else "weak",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": {"workload": wl.name, "path": "numpy.fft (pocketfft) float64, the reference's python/spectral/reference.py"},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},

@@ -164,6 +164,14 @@ void need(bool ok, const std::string& message)
     }
 }
 
+// True when the byte ranges [a, a + an) and [b, b + bn) share a byte.
+bool overlap(const void* a, unsigned long long an, const void* b, unsigned long long bn)
+{
+    const auto pa = reinterpret_cast<unsigned long long>(a);
+    const auto pb = reinterpret_cast<unsigned long long>(b);
+    return an > 0 && bn > 0 && pa < pb + bn && pb < pa + an;
+}
+
 void need_aligned(const void* p, const char* who)
 {
     need((reinterpret_cast<unsigned long long>(p) & 7u) == 0, std::string(who) + ": arrays must be 8-byte aligned");
@@ -251,6 +259,10 @@ extern "C" int spectral_spectrum(const char* impl, const void* x, const float* w
     using namespace spectral;
     return rf_guarded([&] {
         check_common("spectrum", n, nfft, rows);
+        // Frames are read and written by different CTAs: the output may not share memory with
+        // the signal.
+        const unsigned long long frames = n <= 0 ? 1 : (n + nfft - 1) / nfft;
+        need(!overlap(x, 8ULL * rows * n, y, 8ULL * rows * frames * nfft), "spectrum: x and y must not overlap");
         need_aligned(x, "spectrum");
         need_aligned(y, "spectrum");
         with_variant(impl, "spectrum", [&](auto b_, auto table_) {
@@ -272,7 +284,8 @@ extern "C" int spectral_fir(const char* impl, const void* x, const void* taps_sp
         check_common("fir", n, nfft, rows);
         need(taps >= 1 && taps <= nfft, "fir: nfft must be a power of two of at least len(taps) = "
                                             + std::to_string(taps) + ", got " + std::to_string(nfft));
-        need(n == 0 || rows == 0 || x != y, "fir: x and y must not overlap");
+        // A block reads m - 1 samples that the previous block writes: no overlap at all.
+        need(!overlap(x, 8ULL * rows * n, y, 8ULL * rows * n), "fir: x and y must not overlap");
         need_aligned(x, "fir");
         need_aligned(y, "fir");
         need_aligned(taps_spectrum, "fir");

@@ -74,9 +74,11 @@ def test_unknown_implementation_is_rejected_by_name():
         ("spectral_c2c_pruned", (b"stockham_r8", 0, 0, 8, 9, 1, 0, 0, None), "keep must be in"),
         ("spectral_c2c", (b"stockham_r8", 4096, 4096, 8, 2, 0, None), "must not overlap"),
         ("spectral_spectrum", (b"stockham_r8", 0, 0, 0, 100, 12, 1, None), "power of two from 2 to 4096"),
-        ("spectral_spectrum", (b"naive", 0, 0, 0, 100, 64, 1, None), "no fused kernel"),
+        ("spectral_spectrum", (b"naive", 4096, 0, 1 << 20, 100, 64, 1, None), "no fused kernel"),
         ("spectral_fir", (b"stockham_r8", 0, 0, 0, 100, 64, 65, 1, None), "at least len\\(taps\\) = 65"),
         ("spectral_fir", (b"stockham_r8", 4096, 0, 4096, 100, 64, 8, 1, None), "must not overlap"),
+        ("spectral_fir", (b"stockham_r8", 4096, 0, 4104, 100, 64, 8, 1, None), "must not overlap"),
+        ("spectral_spectrum", (b"stockham_r8", 4096, 0, 4096 + 8 * 50, 100, 64, 1, None), "must not overlap"),
         ("spectral_fir", (b"stockham_r8", 0, 0, 0, 100, 8192, 8, 1, None), "power of two from 2 to 4096"),
     ],
 )

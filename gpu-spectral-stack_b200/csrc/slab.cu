@@ -419,6 +419,14 @@ __global__ void __launch_bounds__(256) slab_relayout_kernel(const BlockTable t, 
     }
 }
 
+// True when the byte ranges [a, a + an) and [b, b + bn) share a byte.
+bool overlap(const void* a, unsigned long long an, const void* b, unsigned long long bn)
+{
+    const auto pa = reinterpret_cast<unsigned long long>(a);
+    const auto pb = reinterpret_cast<unsigned long long>(b);
+    return an > 0 && bn > 0 && pa < pb + bn && pb < pa + an;
+}
+
 void check_aligned(const void* p)
 {
     if ((reinterpret_cast<unsigned long long>(p) & 7u) != 0) {
@@ -540,7 +548,8 @@ extern "C" int spectral_slab_twiddle_columns(const void* x, void* y, int n1, int
         if (width < 1 || col0 < 0 || col0 + width > n / n1) {
             throw InvalidArgument("slab_twiddle_columns: the slab's columns must lie in 0 .. n/n1 - 1");
         }
-        if (x == y) {
+        const unsigned long long bytes = 8ULL * n1 * width;
+        if (overlap(x, bytes, y, bytes)) {
             throw InvalidArgument("slab_twiddle_columns: x and y must not overlap");
         }
         check_aligned(x);
@@ -566,7 +575,8 @@ extern "C" int spectral_transpose(const void* x, void* y, int rows, int cols, lo
         if (rows < 1 || cols < 1 || batch < 0) {
             throw InvalidArgument("transpose: need rows, cols >= 1 and batch >= 0");
         }
-        if (x == y) {
+        const unsigned long long bytes = 8ULL * rows * cols * static_cast<unsigned long long>(batch);
+        if (x == y || overlap(x, bytes, y, bytes)) {
             throw InvalidArgument("transpose: x and y must not overlap");
         }
         check_aligned(x);

@@ -51,6 +51,10 @@ import numpy as np  # noqa: E402
 METRIC = "Effective FFT GB/s (% of B200 HBM peak) at 2^24 pts/GPU, 1/2/4/8 GPUs"
 UNIT = "GB/s"
 SETS = 4
+MIN_ROUNDS = 5           # timed rounds of K steps at least (the reference's default)
+MAX_ROUNDS = 400
+ROUND_TARGET_MS = 40.0   # rounds enough for ~20 NVML clock samples under load
+SPREAD_WARN = 0.05       # (max - min) / median of the rounds above this gets a warning
 
 
 def parse() -> argparse.Namespace:
@@ -130,6 +134,17 @@ class Real:
     def cpu_rows_bytes(self, rows: int) -> int:
         return 2 * rows * (4 * self.n + 8 * self.w)
 
+    def parity(self, sets) -> dict:
+        """Set 0 after the timed steps: its spectrum (rfft of x) and its y (irfft of that
+        spectrum), on a sample of rows, against the oracle applied to the same inputs."""
+        from oracle import reference as ref
+
+        x, s, y = sets[0]
+        rows = sample_rows(self.batch)
+        xh, sh, yh = (t[rows].cpu().numpy() for t in (x, s, y))
+        return parity_line(self.n, [("rfft", sh, ref.rfft(xh)), ("irfft", yh, ref.irfft(sh, self.n))],
+                           len(rows))
+
 
 class C2c:
     """fft_c2c forward then inverse, n = 1024, batch = 16384, complex64 N(0, 1)."""
@@ -177,6 +192,14 @@ class C2c:
 
     def cpu_rows_bytes(self, rows):
         return 2 * 16 * rows * self.n
+
+    def parity(self, sets) -> dict:
+        from oracle import reference as ref
+
+        x, f, y = sets[0]
+        rows = sample_rows(self.batch)
+        xh, fh, yh = (t[rows].cpu().numpy() for t in (x, f, y))
+        return parity_line(self.n, [("fft", fh, ref.fft(xh)), ("ifft", yh, ref.ifft(fh))], len(rows))
 
 
 class Rfft2:
@@ -233,6 +256,16 @@ class Rfft2:
 
     def cpu_step(self, ref, x):
         ref.irfft2(ref.rfft2(x), (self.n1, self.n2))
+
+    def parity(self, sets) -> dict:
+        from oracle import reference as ref
+
+        x, s, y = sets[0]
+        rows = sample_rows(self.batch, 16)
+        xh, sh, yh = (t[rows].cpu().numpy() for t in (x, s, y))
+        n = self.n1 * self.n2
+        return parity_line(n, [("rfft2", sh, ref.rfft2(xh)), ("irfft2", yh, ref.irfft2(sh, (self.n1, self.n2)))],
+                           len(rows), axes=(-2, -1))
 
     def cpu_rows_bytes(self, rows):
         return 2 * rows * (4 * self.n1 * self.n2 + 8 * self.n1 * self.w)
@@ -307,6 +340,27 @@ class Pruned:
     def cpu_step(self, ref, x):
         modes = ref.rfft2_truncate(x, self.m, self.m)
         ref.irfft2_from_modes(modes, (self.n, self.n))
+
+    def parity(self, sets) -> dict:
+        """Set 0: its modes (rfft2_truncated of x), its contraction and its output (the inverse of
+        the contraction), on a sample of samples, each stage against the oracle applied to that
+        stage's own input."""
+        from oracle import reference as ref
+        from oracle.policy import relative_error
+
+        x, modes, mixed, y = sets[0]
+        rows = sample_rows(self.samples, 4)
+        xh, mh, ch, yh = (t[rows].cpu().numpy() for t in (x, modes, mixed, y))
+        n = self.n * self.n
+        line = parity_line(n, [("rfft2_truncated", mh, ref.rfft2_truncate(xh, self.m, self.m)),
+                               ("irfft2_from_modes", yh, ref.irfft2_from_modes(ch, (self.n, self.n)))],
+                           len(rows), axes=(-2, -1))
+        expected = ref.mode_contract(mh, self.weights.cpu().numpy())
+        err = float(np.max(relative_error(ch.reshape(*ch.shape[:2], -1), expected.reshape(*ch.shape[:2], -1), (-1,))))
+        ctol = 2 * float(np.finfo(np.float32).eps) * (math.log2(self.channels) + 1)
+        line["stages"]["mode_contract"] = {"max_rel_err": err, "tol": ctol}
+        line["ok"] = line["ok"] and err <= ctol
+        return line
 
     def cpu_rows_bytes(self, rows):  # rows = samples
         return 2 * rows * self.channels * (4 * self.n * self.n + 16 * self.m * self.m)
@@ -835,6 +889,30 @@ def make_workload(args):
     return Pruned(args.fft_impl)
 
 
+# --- parity of the timed outputs ------------------------------------------------------------------
+
+
+def sample_rows(count: int, want: int = 64) -> list[int]:
+    """`want` indices spread evenly over `count` rows (first and last included)."""
+    if count <= want:
+        return list(range(count))
+    return sorted({round(i * (count - 1) / (want - 1)) for i in range(want)})
+
+
+def parity_line(n: int, stages, rows: int, axes=(-1,)) -> dict:
+    """Worst relative L2 error per transform of each stage against the oracle, with the
+    tolerance 2 eps log2 N of oracle/policy.py."""
+    from oracle.policy import fft_tolerance, relative_error
+
+    tol = fft_tolerance(n)
+    out = {}
+    for name, actual, expected in stages:
+        out[name] = {"max_rel_err": float(np.max(relative_error(actual, expected, axes))), "tol": tol}
+    worst = max(v["max_rel_err"] for v in out.values())
+    return {"max_rel_err": worst, "tol": tol, "rows": rows, "ok": all(v["max_rel_err"] <= v["tol"] for v in out.values()),
+            "stages": out, "checked": "the timed steps' outputs of buffer set 0 against the float64 oracle"}
+
+
 # --- peaks, clocks, profiles ---------------------------------------------------------------------
 
 
@@ -860,6 +938,31 @@ def ncu_traffic(kernel: str, workload: str) -> float | None:
                 except ValueError:
                     return None
     return None
+
+
+def fp32_ceiling(native, stream) -> float:
+    """The GPU's FP32 ceiling in TFLOP/s: the faster of the scalar-FFMA and packed-FFMA2 forms of
+    spectral_fp32_ceiling, each the median of 5 timed launches after 2 warm-up launches."""
+    import ctypes
+
+    import torch
+
+    sink = torch.zeros(1, dtype=torch.float32, device="cuda")
+    best = 0.0
+    for packed in (0, 1):
+        flops = ctypes.c_double(0.0)
+        times = []
+        for i in range(7):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            native.call("spectral_fp32_ceiling", sink.data_ptr(), 2048, packed, stream.cuda_stream,
+                        ctypes.byref(flops))
+            b.record(stream)
+            b.synchronize()
+            if i >= 2:
+                times.append(a.elapsed_time(b))
+        best = max(best, flops.value / (statistics.median(times) * 1e-3) / 1e12)
+    return best
 
 
 class ClockSampler:
@@ -1043,22 +1146,51 @@ def run_ours(args) -> None:
         step(k)
     torch.cuda.synchronize()
 
-    start = torch.cuda.Event(enable_timing=True)
-    stop = torch.cuda.Event(enable_timing=True)
+    # Rounds: the K timed steps are measured as a round, repeated back to back (the reference's
+    # protocol: median of rounds, min and max beside it, a warning above 5 % spread; its
+    # csrc/common/bench.cpp:48-81). Enough rounds run for the clock sampler to see the GPU
+    # under load at least ~20 times (about 40 ms of timed work), and at least 5. Every rank runs
+    # the same number of rounds; each round's time is the slowest rank's.
+    probe = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    probe[0].record(stream)
+    for k in range(args.steps):
+        step(k)
+    probe[1].record(stream)
+    torch.cuda.synchronize()
+    est_round_ms = max(probe[0].elapsed_time(probe[1]), 1e-3)
+    rounds = int(min(MAX_ROUNDS, max(MIN_ROUNDS, math.ceil(ROUND_TARGET_MS / est_round_ms))))
+    if world > 1:
+        r = torch.tensor([rounds], dtype=torch.int64, device="cuda")
+        dist.all_reduce(r, op=dist.ReduceOp.MAX)
+        rounds = int(r.item())
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(rounds + 1)]
+
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     # The timed region holds the steps alone: an event recorded between two kernels costs a few
-    # microseconds of its own (it breaks the back-to-back launch of the next kernel).
+    # microseconds of its own (it breaks the back-to-back launch of the next kernel), so events
+    # sit only between rounds.
     with ClockSampler(local) as clocks:
-        start.record(stream)
-        for k in range(args.steps):
-            step(k)
-        stop.record(stream)
+        marks[0].record(stream)
+        for r in range(rounds):
+            for k in range(args.steps):
+                step(r * args.steps + k)
+            marks[r + 1].record(stream)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    elapsed_ms = start.elapsed_time(stop)
+    round_ms = torch.tensor([marks[r].elapsed_time(marks[r + 1]) for r in range(rounds)],
+                            dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(round_ms, op=dist.ReduceOp.MAX)
+    round_ms = round_ms.cpu().tolist()
+    max_ms = statistics.median(round_ms)  # the median round, slowest rank per round
+    spread = (max(round_ms) - min(round_ms)) / max_ms
+    if spread > SPREAD_WARN and rank == 0:
+        print(f"warning: rounds spread {100 * spread:.1f} % (min {min(round_ms):.4f} ms, max "
+              f"{max(round_ms):.4f} ms per {args.steps} steps)", file=sys.stderr)
+
     # Per-kernel times for the roofline, from a separate pass with an event around every launch.
     pk = min(args.steps, 100)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(kernels) + 1)] for _ in range(pk)]
@@ -1067,12 +1199,14 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     per_kernel_ms = [statistics.mean(ev[k][j].elapsed_time(ev[k][j + 1]) for k in range(pk))
                      for j in range(len(kernels))]
-    t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
     bytes_per_step = sum(b for _, b in kernels)
     value = world * bytes_per_step * args.steps / (max_ms * 1e-3) / 1e9
+    timing = {"rounds": rounds, "steps_per_round": args.steps, "statistic": "median round",
+              "round_ms_median": round(max_ms, 5), "round_ms_min": round(min(round_ms), 5),
+              "round_ms_max": round(max(round_ms), 5), "spread": round(spread, 4),
+              "spread_warning": spread > SPREAD_WARN,
+              "value_min": round(world * bytes_per_step * args.steps / (max(round_ms) * 1e-3) / 1e9, 3),
+              "value_max": round(world * bytes_per_step * args.steps / (min(round_ms) * 1e-3) / 1e9, 3)}
 
     # The dominant kernel: the largest share of device time. Its average launch duration inside
     # the timed region is the region's time per step times its share, the shares taken from the
@@ -1146,6 +1280,24 @@ def run_ours(args) -> None:
                "one_core": {"value": round(bytes_one / t_one / 1e9, 3), "unit": UNIT,
                             "sample": f"{rows1} rows, best of 3, 1 thread"}}
 
+    # The outputs the timed steps left in buffer set 0, against the oracle on a row sample (rank
+    # 0; every rank's kernels are the same).
+    parity = wl.parity(sets) if rank == 0 and hasattr(wl, "parity") else None
+    if parity is not None and not parity["ok"]:
+        print(f"error: timed outputs outside tolerance: {json.dumps(parity)}", file=sys.stderr)
+
+    # The contraction is bound by FP32 issue, not HBM: its roofline uses the measured FP32
+    # ceiling (spectral_fp32_ceiling) and the contraction's 8 cin cout flops per mode and sample.
+    fp32 = None
+    if isinstance(wl, Pruned):
+        ceiling = fp32_ceiling(native, stream)
+        j = [n for n, _ in kernels].index("mode_contract")
+        flops = 8.0 * wl.samples * wl.channels * wl.channels * 2 * wl.m * wl.m
+        tf = flops / (in_step_ms[j] * 1e-3) / 1e12
+        fp32 = {"bound": "fp32", "kernel": "mode_contract", "achieved": round(tf, 2),
+                "peak": round(ceiling, 2), "unit": "TFLOP/s", "frac": round(tf / ceiling, 4),
+                "flops": flops, "peak_source": "measured in this run (spectral_fp32_ceiling)"}
+
     faults = native.device_faults()
     if world > 1:
         dist.destroy_process_group()
@@ -1161,9 +1313,12 @@ def run_ours(args) -> None:
                    "l2": "4 rotating buffer sets (6x L2); inverse reads a spectrum written 2 steps earlier",
                    "pct_hbm_peak": round(100 * value / world / peak, 2)},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": args.steps * wl.launches_per_step(),
-        "clocks": clocks.summary(), "device_faults": faults, "impl": "ours",
+        "gpu_launches": rounds * args.steps * wl.launches_per_step(),
+        "clocks": clocks.summary(), "timing": timing, "parity": parity, "device_faults": faults,
+        "impl": "ours",
     }
+    if fp32 is not None:
+        line["fp32_roofline"] = fp32
     print(json.dumps(line), flush=True)
 
 

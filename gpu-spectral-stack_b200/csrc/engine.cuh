@@ -568,8 +568,9 @@ __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
             // bounded) so nothing lands in shared memory after the CTA is gone, and stop.
             if (threadIdx.x == 0) {
                 atomicOr(fault, tma::kFaultWaitTimeout);
-                if (tf0 + stride < batch) {
-                    tma::mbar_wait(&bars[s ^ 1], static_cast<unsigned>((j + 1) >> 1) & 1u);
+                if (tf0 + stride < batch
+                    && !tma::mbar_wait(&bars[s ^ 1], static_cast<unsigned>((j + 1) >> 1) & 1u)) {
+                    atomicOr(fault, tma::kFaultDrainTimeout);
                 }
             }
             return;

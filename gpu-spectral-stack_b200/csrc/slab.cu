@@ -475,6 +475,12 @@ extern "C" int spectral_slab_rows(const void* x, void* y, int n, long long rows,
         if (rows < 1 || rows > INT_MAX) {
             throw InvalidArgument("fft2_slab: rows must be from 1 to INT_MAX");
         }
+        // A CTA stores its row's chunks where other rows' inputs lie (ranks > 1), so any overlap
+        // of x and y races between CTAs: out of place only.
+        const unsigned long long bytes = 8ULL * static_cast<unsigned long long>(rows) * static_cast<unsigned>(n);
+        if (overlap(x, bytes, y, bytes)) {
+            throw InvalidArgument("fft2_slab: the row stage is out of place (x and y must not overlap)");
+        }
         const auto* xs = static_cast<const float2*>(x);
         auto* ys = static_cast<float2*>(y);
         const auto s = static_cast<cudaStream_t>(stream);
@@ -615,6 +621,18 @@ extern "C" int spectral_slab_relayout(const void* const* src, void* const* dst, 
             t.src[r] = static_cast<const float2*>(src[r]);
             t.dst[r] = static_cast<float2*>(dst[r]);
         }
+        // Threads of different CTAs copy different blocks: a source block that shares memory
+        // with any destination block races, so every pair is refused (at most 16 x 16).
+        const unsigned long long src_bytes = 8ULL * (static_cast<unsigned long long>(h - 1) * src_stride + w);
+        const unsigned long long dst_bytes = 8ULL * (static_cast<unsigned long long>(h - 1) * dst_stride + w);
+        for (int r = 0; r < ranks; ++r) {
+            for (int q = 0; q < ranks; ++q) {
+                if (overlap(src[r], src_bytes, dst[q], dst_bytes)) {
+                    throw InvalidArgument("slab_relayout: source block " + std::to_string(r)
+                                          + " overlaps destination block " + std::to_string(q));
+                }
+            }
+        }
         const long long per_rank = static_cast<long long>(h) * (pairs ? w / 2 : w);
         const long long blocks_x = (per_rank + 255) / 256;
         const dim3 grid(static_cast<unsigned>(blocks_x < 4096 ? blocks_x : 4096), static_cast<unsigned>(ranks));
@@ -637,8 +655,11 @@ extern "C" int spectral_slab_columns(void* x, void* y, int n, int width, int inv
         if (width < 1) {
             throw InvalidArgument("fft2_slab: width must be at least 1");
         }
-        if (x == y) {
-            throw InvalidArgument("fft2_slab: columns are transformed out of place (x != y)");
+        // For n > 4096 the first pass writes x and the second reads x and writes y: any overlap
+        // of the two, not only x == y, would corrupt the result.
+        const unsigned long long bytes = 8ULL * static_cast<unsigned>(n) * static_cast<unsigned>(width);
+        if (overlap(x, bytes, y, bytes)) {
+            throw InvalidArgument("fft2_slab: columns are transformed out of place (x and y must not overlap)");
         }
         auto* xs = static_cast<float2*>(x);
         auto* ys = static_cast<float2*>(y);

@@ -21,6 +21,7 @@ constexpr unsigned kSpinLimit = 1u << 22;
 
 // Fault codes, OR-ed into the fault word.
 constexpr unsigned kFaultWaitTimeout = 1u;
+constexpr unsigned kFaultDrainTimeout = 2u;  // the wait for an abandoned copy also gave up
 
 __device__ __forceinline__ unsigned smem_addr(const void* p)
 {
@@ -75,10 +76,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity)
     return ok != 0;
 }
 
-// Waits for phase `parity` of `bar` to complete; false if it did not within the limit.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity)
+// Completes `bytes` of the current phase's expected transaction count without a copy: what a
+// copy that will never come would have delivered. Used to drain a phase after a wait gave up.
+__device__ __forceinline__ void mbar_complete_tx(uint64_t* bar, unsigned bytes)
 {
-    for (unsigned i = 0; i < kSpinLimit; ++i) {
+    asm volatile("mbarrier.complete_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// Waits for phase `parity` of `bar` to complete; false if it did not within `limit` polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned limit = kSpinLimit)
+{
+    for (unsigned i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, parity)) {
             return true;
         }

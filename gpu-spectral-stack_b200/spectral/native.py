@@ -35,6 +35,7 @@ _ip = ctypes.POINTER(ctypes.c_int)
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_last_error": (_s, []),
     "spectral_device_faults": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
+    "spectral_probe_bounded_wait": (_i, [_p, _p, ctypes.c_uint, ctypes.c_uint, _p]),
     "spectral_impl_count": (_i, []),
     "spectral_impl_name": (_s, [_i]),
     "spectral_impl_find": (_i, [_s]),
@@ -75,6 +76,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_ipc_close": (_i, [_p]),
     "spectral_ipc_free": (_i, [_p]),
     "spectral_mode_contract": (_i, [_p, _p, _p, _ll, _i, _i, _ll, _p]),
+    "spectral_fp32_ceiling": (_i, [_p, _i, _i, _p, ctypes.POINTER(ctypes.c_double)]),
     "spectral_spectrum": (_i, [_s, _p, _p, _p, _ll, _i, _ll, _p]),
     "spectral_fir": (_i, [_s, _p, _p, _p, _ll, _i, _i, _ll, _p]),
     "spectral_flow_workspace": (_i, [_i, _i, _ll, _szp]),

@@ -53,7 +53,19 @@ SPECTRAL_API const char* spectral_last_error(void);
  * asynchronous copy gave up records SPECTRAL_FAULT_WAIT_TIMEOUT and returns instead of hanging.
  * No counterpart in the reference, whose kernels have no waits. */
 #define SPECTRAL_FAULT_WAIT_TIMEOUT 1u
+#define SPECTRAL_FAULT_DRAIN_TIMEOUT 2u /* the wait for a copy still in flight also gave up */
 SPECTRAL_API int spectral_device_faults(unsigned* faults, int clear);
+
+/* Test hook for the bounded-wait path above (no counterpart in the reference). One CTA stages
+ * 1 KiB from `src` into shared memory with one bulk copy completing on an mbarrier and waits for
+ * it with the library's bounded wait, as the staged row kernel does, then writes the staged
+ * bytes to `dst`. With missing_bytes > 0 (a multiple of 16, at most 1 MiB) the barrier expects
+ * that many bytes more than the copy delivers, so the wait gives up after spin_limit polls and
+ * records SPECTRAL_FAULT_WAIT_TIMEOUT; the probe then completes the missing bytes itself and
+ * waits (bounded) for the real copy to land before returning. With missing_bytes == 0 it records
+ * nothing. src and dst: 1 KiB each, 16-byte aligned. Nothing faults or waits without a limit. */
+SPECTRAL_API int spectral_probe_bounded_wait(const void* src, void* dst, unsigned missing_bytes,
+                                             unsigned spin_limit, void* stream);
 
 /* --- registry (reference: csrc/fft/registry.hpp:14-51, csrc/torch/ops.cpp:422-438) --------- */
 
@@ -166,8 +178,9 @@ SPECTRAL_API int spectral_irfft2_modes(const char* impl, const void* modes, floa
  * all-to-all of its row blocks, then spectral_slab_rows(inverse) from the received chunks. */
 SPECTRAL_API int spectral_slab_rows(const void* x, void* y, int n, long long rows, int ranks,
                                     int inverse, void* stream);
-/* n-point transforms down every column of the n x width row-major matrix x, into y (natural
- * order, same layout). x is used as scratch for n > 4096 and must not be y. */
+/* (spectral_slab_rows is out of place: x and y, rows x n values each, must not overlap.)
+ * n-point transforms down every column of the n x width row-major matrix x, into y (natural
+ * order, same layout). x is used as scratch for n > 4096; x and y must not overlap. */
 SPECTRAL_API int spectral_slab_columns(void* x, void* y, int n, int width, int inverse,
                                        void* stream);
 
@@ -192,6 +205,7 @@ SPECTRAL_API int spectral_slab_rows_peer(const void* x, void* y, void* const* pe
  * the natural w x n rows. Before an inverse, src[r] = x + r w (stride n) and dst[r] = send +
  * r w^2 (stride w) pack the send blocks. src[r] may be another rank's buffer mapped through
  * CUDA IPC (plain NVLink loads), which fuses the exchange into the copy. */
+/* No source block may share memory with any destination block (checked). */
 SPECTRAL_API int spectral_slab_relayout(const void* const* src, void* const* dst, int ranks, int h, int w,
                                         long long src_stride, long long dst_stride, void* stream);
 
@@ -249,6 +263,15 @@ SPECTRAL_API int spectral_ipc_free(void* ptr);
  * reference plans it (docs/ROADMAP.md:71-76, tasks 3.3-3.6) but has no implementation. */
 SPECTRAL_API int spectral_mode_contract(const void* x, const void* w, void* out, long long batch, int cin,
                            int cout, long long modes, void* stream);
+
+/* The FP32 arithmetic ceiling, for the roofline of FP32-bound kernels such as the contraction
+ * (reference: csrc/tools/peaks.cu:46-70, a separate tool there). Launches one full wave of CTAs
+ * that run independent fused multiply-add chains and nothing else: scalar FFMA (packed == 0) or
+ * Blackwell's packed FP32x2 FFMA2 (packed != 0), `iters` trips of 128 chain steps per thread.
+ * *flops receives the floating-point operations the launch performs (2 per FFMA, 4 per FFMA2);
+ * the caller times the launch on `stream`. sink: one float, written only by a test the compiler
+ * cannot fold (never true in practice). */
+SPECTRAL_API int spectral_fp32_ceiling(float* sink, int iters, int packed, void* stream, double* flops);
 
 /* --- radio signals: windowed spectrum and overlap-save FIR (reference: python/spectral/rf.py) -- */
 

@@ -150,3 +150,32 @@ def test_slab_relayout_argument_checks():
         native.call("spectral_slab_twiddle_columns", 8, 16, 64, 8, 60, 4096, 0, None)
     with pytest.raises(ValueError, match="must not overlap"):
         native.call("spectral_transpose", 8, 8, 4, 4, 1, None)
+
+
+@pytest.mark.parametrize(
+    ("fn", "args"),
+    [
+        # (x, y) one value apart: a partial overlap, not the same pointer.
+        ("spectral_slab_twiddle_columns", (4096, 4104, 64, 8, 0, 4096, 0, None)),
+        ("spectral_transpose", (4096, 4104, 4, 4, 1, None)),
+        ("spectral_slab_rows", (4096, 4104, 8, 8, 2, 0, None)),
+        ("spectral_slab_rows", (4096, 4096, 8, 8, 1, 1, None)),
+        ("spectral_slab_columns", (4096, 4104, 8, 8, 0, None)),
+        ("spectral_slab_columns", (4096 + 8 * 63, 4096, 8, 8, 1, None)),
+    ],
+)
+def test_overlapping_input_and_output_ranges_are_refused(fn, args):
+    # Every check runs before any CUDA call, so the fake pointers never reach a kernel.
+    with pytest.raises(ValueError, match="must not overlap"):
+        native.call(fn, *args)
+
+
+def test_slab_relayout_refuses_a_source_block_that_overlaps_any_destination_block():
+    import ctypes
+
+    # Two 4 x 4 blocks: source block 1 (rows of stride 4 from 4096 + 128) shares its last row with
+    # destination block 0 (from 4096 + 224); sources and destinations are otherwise disjoint.
+    src = (ctypes.c_void_p * 2)(4096, 4096 + 128)
+    dst = (ctypes.c_void_p * 2)(4096 + 224, 8192)
+    with pytest.raises(ValueError, match="source block 1 overlaps destination block 0"):
+        native.call("spectral_slab_relayout", src, dst, 2, 4, 4, 4, 4, None)

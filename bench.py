@@ -72,7 +72,14 @@ def parse() -> argparse.Namespace:
                    help="slab workload on 2+ GPUs: row kernel stores into the peers' memory, or an NCCL all-to-all")
     p.add_argument("--layout", choices=["columns", "natural"], default="columns",
                    help="slab workload: leave the column slab (one exchange) or return natural rows (two)")
+    p.add_argument("--rounds", type=int, default=0,
+                   help="timed rounds of K steps (0: enough for ~40 ms of timed work, at least 5)")
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    p.add_argument("--sweep", action="store_true",
+                   help="time every operation x implementation x size at 2^24 points per call and write the "
+                        "reference's CSV (spectral.benchmark) instead of the JSON line")
+    p.add_argument("--sweep-out", default="", help="--sweep: CSV path (default: standard output)")
+    p.add_argument("--sweep-ops", default="all", help="--sweep: comma-separated operations, or all")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     return p.parse_args()
 
@@ -1159,6 +1166,8 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     est_round_ms = max(probe[0].elapsed_time(probe[1]), 1e-3)
     rounds = int(min(MAX_ROUNDS, max(MIN_ROUNDS, math.ceil(ROUND_TARGET_MS / est_round_ms))))
+    if args.rounds > 0:
+        rounds = args.rounds
     if world > 1:
         r = torch.tensor([rounds], dtype=torch.int64, device="cuda")
         dist.all_reduce(r, op=dist.ReduceOp.MAX)
@@ -1286,17 +1295,23 @@ def run_ours(args) -> None:
     if parity is not None and not parity["ok"]:
         print(f"error: timed outputs outside tolerance: {json.dumps(parity)}", file=sys.stderr)
 
-    # The contraction is bound by FP32 issue, not HBM: its roofline uses the measured FP32
-    # ceiling (spectral_fp32_ceiling) and the contraction's 8 cin cout flops per mode and sample.
-    fp32 = None
+    # The contraction runs on the tensor cores (split TF32) where its shape fits: its own line
+    # gives its time against the HBM floor of its bytes, and its useful FLOP rate against the
+    # measured FP32 ceiling (spectral_fp32_ceiling), the rate an FP32 kernel could at most reach.
+    contraction = None
     if isinstance(wl, Pruned):
         ceiling = fp32_ceiling(native, stream)
         j = [n for n, _ in kernels].index("mode_contract")
+        us = in_step_ms[j] * 1e3
         flops = 8.0 * wl.samples * wl.channels * wl.channels * 2 * wl.m * wl.m
-        tf = flops / (in_step_ms[j] * 1e-3) / 1e12
-        fp32 = {"bound": "fp32", "kernel": "mode_contract", "achieved": round(tf, 2),
-                "peak": round(ceiling, 2), "unit": "TFLOP/s", "frac": round(tf / ceiling, 4),
-                "flops": flops, "peak_source": "measured in this run (spectral_fp32_ceiling)"}
+        tf = flops / (us * 1e-6) / 1e12
+        gbs = wl.contract_bytes / (us * 1e-6) / 1e9
+        contraction = {"kernel": "mode_contract", "method": "tensor cores, split TF32 (tcgen05)",
+                       "us_in_step": round(us, 2), "bytes": wl.contract_bytes,
+                       "hbm": {"achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4)},
+                       "useful_flops": flops, "useful_tflops": round(tf, 2),
+                       "fp32_ceiling_tflops": round(ceiling, 2), "vs_fp32_ceiling": round(tf / ceiling, 4),
+                       "fp32_ceiling_source": "measured in this run (spectral_fp32_ceiling)"}
 
     faults = native.device_faults()
     if world > 1:
@@ -1317,13 +1332,130 @@ def run_ours(args) -> None:
         "clocks": clocks.summary(), "timing": timing, "parity": parity, "device_faults": faults,
         "impl": "ours",
     }
-    if fp32 is not None:
-        line["fp32_roofline"] = fp32
+    if contraction is not None:
+        line["contraction"] = contraction
     print(json.dumps(line), flush=True)
+
+# --- the sweep: every operation x implementation x size ----------------------------------------
+
+SWEEP_OPS = ("fft_c2c", "fft_r2c", "fft_c2r", "fft2_c2c", "fft2_r2c", "fft2_c2r", "rfft2_modes", "irfft2_modes",
+             "scale")
+SWEEP_POINTS = 1 << 24
+
+
+def run_sweep(args) -> None:
+    """The reference's spectral_bench sweep (its csrc/tools/spectral_bench.cpp:509-575) on this
+    library: for each operation, implementation and power-of-two size 2 .. 4096 (2D: n x n
+    arrays), batch = 2^24 / points per transform; time_cuda's median of 5 rounds of 20 calls, 4
+    rotating buffer sets of 2^24 points each (twice the 126 MB L2 per set); one CSV row each,
+    columns of spectral.benchmark. Rows whose rounds spread by more than 5 % are listed on
+    standard error."""
+    import torch
+
+    import spectral
+    from spectral import benchmark as bm
+    from spectral import native
+
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "ours", "unavailable": "no CUDA device visible"}))
+        return
+    ops = SWEEP_OPS if args.sweep_ops == "all" else tuple(args.sweep_ops.split(","))
+    unknown = set(ops) - set(SWEEP_OPS)
+    if unknown:
+        raise SystemExit(f"--sweep-ops: unknown operations {sorted(unknown)}; choose from {SWEEP_OPS}")
+    peak, peak_source = hbm_peak()
+    stream = torch.cuda.current_stream().cuda_stream
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    sets = [(torch.randn(SWEEP_POINTS, dtype=torch.complex64, device="cuda", generator=gen),
+             torch.empty(SWEEP_POINTS + 4096, dtype=torch.complex64, device="cuda")) for _ in range(SETS)]
+    work = torch.empty(2 * SWEEP_POINTS + 4096, dtype=torch.complex64, device="cuda")
+    impls = [n for n in spectral.FFT_IMPLS]
+    sizes = [1 << k for k in range(1, 13)]
+    results = []
+
+    def timed(op, impl, n, batch, flops_bytes, launch):
+        try:
+            t = bm.time_cuda(launch, arg_sets=[(x.data_ptr(), y.data_ptr()) for x, y in sets])
+        except ValueError as e:  # the implementation does not take this shape
+            print(f"skipped {op} {impl} n={n}: {e}", file=sys.stderr)
+            return
+        flops, nbytes = flops_bytes
+        results.append(bm.Result(op, impl, n, batch, t, flops, nbytes))
+        if t.spread > SPREAD_WARN:
+            print(f"warning: {op} {impl} n={n} batch={batch}: rounds spread {100 * t.spread:.1f} %", file=sys.stderr)
+
+    def limits(impl):
+        import ctypes
+
+        v = [ctypes.c_int(0) for _ in range(6)]
+        native.call("spectral_impl_limits", impl.encode(), *[ctypes.byref(a) for a in v])
+        return [a.value for a in v]  # max_n, max_c2c_n, max_real_n, has_columns, has_pruned, needs_work
+
+    for op in ops:
+        for impl in impls:
+            imp = impl.encode()
+            max_n, max_c2c, max_real, has_columns, _, _ = limits(impl)
+            if op == "scale":
+                if impl == impls[0]:
+                    timed("scale", "ours", SWEEP_POINTS, 1, (2.0 * SWEEP_POINTS, 16.0 * SWEEP_POINTS),
+                          lambda x, y: native.call("spectral_scale", x, y, SWEEP_POINTS, 0.5, stream))
+                continue
+            for n in sizes:
+                if op == "fft_c2c" and n <= max_c2c:
+                    for inv in (0,):
+                        b = SWEEP_POINTS // n
+                        timed(op, impl, n, b, bm.fft_c2c_work(n, b),
+                              lambda x, y, n=n, b=b: native.call("spectral_c2c", imp, x, y, n, b, inv, stream))
+                elif op in ("fft_r2c", "fft_c2r") and n <= max_real:
+                    b = SWEEP_POINTS // n
+                    fn = "spectral_r2c" if op == "fft_r2c" else "spectral_c2r"
+                    timed(op, impl, n, b, bm.fft_real_work(n, b),
+                          lambda x, y, n=n, b=b, fn=fn: native.call(fn, imp, x, y, n, b, work.data_ptr(), stream))
+                elif op.startswith("fft2_") and n <= max_n and n * n <= SWEEP_POINTS:
+                    b = SWEEP_POINTS // (n * n)
+                    for method, cname in ((1, "strided"), (0, "transpose")):
+                        if method == 1 and not has_columns:
+                            continue
+                        name = f"{impl}/{cname}"
+                        if op == "fft2_c2c":
+                            fb = bm.fft_c2c_work(n * n, b)
+                            call = lambda x, y, n=n, b=b, m=method: native.call(
+                                "spectral_fft2_c2c", imp, m, x, y, n, n, b, 0, work.data_ptr(), stream)
+                        elif op == "fft2_r2c":
+                            fb = bm.fft2_real_work(n, n, b)
+                            call = lambda x, y, n=n, b=b, m=method: native.call(
+                                "spectral_fft2_r2c", imp, m, x, y, n, n, b, work.data_ptr(), stream)
+                        else:
+                            fb = bm.fft2_real_work(n, n, b)
+                            call = lambda x, y, n=n, b=b, m=method: native.call(
+                                "spectral_fft2_c2r", imp, m, x, y, n, n, b, work.data_ptr(), stream)
+                        timed(op, name, n, b, fb, call)
+                elif op in ("rfft2_modes", "irfft2_modes") and 2 <= n <= max_n and n * n <= SWEEP_POINTS:
+                    b = SWEEP_POINTS // (n * n)
+                    m = max(1, n // 8)
+                    fn = "spectral_rfft2_modes" if op == "rfft2_modes" else "spectral_irfft2_modes"
+                    timed(op, impl, n, b, bm.pruned_work(n, n, m, m, b),
+                          lambda x, y, n=n, b=b, m=m, fn=fn: native.call(fn, imp, x, y, n, n, m, m, b, work.data_ptr(), stream))
+    prop = torch.cuda.get_device_properties(0)
+    comments = [f"device: {prop.name}, {prop.multi_processor_count} SMs",
+                f"torch {torch.__version__}, CUDA {torch.version.cuda}",
+                "timing: 3 warm-up calls, then the median over 5 rounds of 20 calls (4 rotating buffer sets of "
+                "2^24 points); times are per call",
+                f"hbm peak {peak} GB/s ({peak_source}); batch = 2^24 / points per transform"]
+    text = bm.format_csv(results, comments, gpus=1, hbm_peak_gbs=peak, peak_source=peak_source,
+                         cpu_cores=os.cpu_count() or "")
+    if args.sweep_out:
+        Path(args.sweep_out).write_text(text)
+        print(json.dumps({"sweep": args.sweep_out, "rows": len(results)}), flush=True)
+    else:
+        sys.stdout.write(text)
 
 
 def main() -> None:
     args = parse()
+    if args.sweep:
+        run_sweep(args)
+        return
     if args.workload == "flow":
         (run_flow_reference if args.impl == "reference" else run_flow)(args)
     elif args.workload == "fft1d" and args.impl == "ours":

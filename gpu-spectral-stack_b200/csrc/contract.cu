@@ -205,6 +205,11 @@ __global__ void __launch_bounds__(256, 2)
     }
 }
 
+// SPECTRAL_CONTRACT_AUTO takes the tensor-core kernel wherever it fits the shape: at the FNO
+// configuration (64 x 64 channels, 512 modes, 64 samples) it measured 27.5 us against 45.6 us for
+// the staged FP32 kernel, both within the FP32 tolerance.
+constexpr bool kAutoTensor = true;
+
 bool staged_fits(const void* x, const void* w, long long batch, int cin, int cout, long long modes)
 {
     const auto aligned = [](const void* p) { return (reinterpret_cast<unsigned long long>(p) & 15u) == 0; };
@@ -214,14 +219,27 @@ bool staged_fits(const void* x, const void* w, long long batch, int cin, int cou
 }
 
 }  // namespace
+
+// The tensor-core contraction (contract_tc.cu).
+bool contract_tc_fits(const void* x, const void* w, const void* out, long long batch, int cin, int cout,
+                      long long modes);
+void contract_tc(const float2* x, const float2* w, float2* out, long long batch, int cin, int cout,
+                 long long modes, cudaStream_t stream);
+
 }  // namespace spectral
 
-extern "C" int spectral_mode_contract(const void* x, const void* w, void* out, long long batch,
-                                      int cin, int cout, long long modes, void* stream)
+namespace {
+
+int mode_contract(const void* x, const void* w, void* out, long long batch, int cin, int cout, long long modes,
+                  int method, void* stream)
 {
     using namespace spectral;
     if (batch < 0 || cin < 1 || cout < 1 || modes < 0 || batch > (1LL << 30)) {
         set_last_error("mode_contract: need batch >= 0, cin >= 1, cout >= 1, modes >= 0");
+        return SPECTRAL_INVALID_ARGUMENT;
+    }
+    if (method < SPECTRAL_CONTRACT_AUTO || method > SPECTRAL_CONTRACT_TENSOR) {
+        set_last_error("mode_contract: method must be SPECTRAL_CONTRACT_AUTO, _FP32 or _TENSOR");
         return SPECTRAL_INVALID_ARGUMENT;
     }
     if (((reinterpret_cast<unsigned long long>(x) | reinterpret_cast<unsigned long long>(w)
@@ -229,7 +247,23 @@ extern "C" int spectral_mode_contract(const void* x, const void* w, void* out, l
         set_last_error("mode_contract: arrays must be 8-byte aligned");
         return SPECTRAL_INVALID_ARGUMENT;
     }
+    const bool tc_fits = contract_tc_fits(x, w, out, batch, cin, cout, modes);
+    if (method == SPECTRAL_CONTRACT_TENSOR && !tc_fits) {
+        set_last_error("mode_contract: the tensor-core method needs batch a multiple of 64, cout of 32, cin of 8 up to 256, "
+                       "modes of 4 and 16-byte aligned arrays");
+        return SPECTRAL_INVALID_ARGUMENT;
+    }
     if (batch == 0 || modes == 0) {
+        return SPECTRAL_OK;
+    }
+    if (method == SPECTRAL_CONTRACT_TENSOR || (method == SPECTRAL_CONTRACT_AUTO && tc_fits && kAutoTensor)) {
+        try {
+            contract_tc(static_cast<const float2*>(x), static_cast<const float2*>(w), static_cast<float2*>(out),
+                        batch, cin, cout, modes, static_cast<cudaStream_t>(stream));
+        } catch (const std::exception& e) {
+            set_last_error(e.what());
+            return SPECTRAL_CUDA_ERROR;
+        }
         return SPECTRAL_OK;
     }
     if (staged_fits(x, w, batch, cin, cout, modes)) {
@@ -270,4 +304,18 @@ extern "C" int spectral_mode_contract(const void* x, const void* w, void* out, l
         return SPECTRAL_CUDA_ERROR;
     }
     return SPECTRAL_OK;
+}
+
+}  // namespace
+
+extern "C" int spectral_mode_contract(const void* x, const void* w, void* out, long long batch,
+                                      int cin, int cout, long long modes, void* stream)
+{
+    return mode_contract(x, w, out, batch, cin, cout, modes, SPECTRAL_CONTRACT_AUTO, stream);
+}
+
+extern "C" int spectral_mode_contract_method(const void* x, const void* w, void* out, long long batch,
+                                             int cin, int cout, long long modes, int method, void* stream)
+{
+    return mode_contract(x, w, out, batch, cin, cout, modes, method, stream);
 }

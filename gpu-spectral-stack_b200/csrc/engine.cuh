@@ -174,6 +174,14 @@ __device__ __forceinline__ float2 computed_half_turn(int k, int n)
     return make_float2(cs, -sn);
 }
 
+// W_M^J = exp(-2 pi i J / M) as a compile-time constant (dft.cuh's cs2pi, rounded once to float).
+template <int J, int M>
+__device__ __forceinline__ float2 wconst()
+{
+    constexpr dft::CosSin w = dft::cs2pi(J, M);
+    return make_float2(static_cast<float>(w.c), -static_cast<float>(w.s));
+}
+
 // Fills the pass tables: computed on chip (Table == false) or copied from `table`.
 template <class PL, bool Table>
 __device__ __forceinline__ void fill_pass_twiddles(float2* tw, const float2* __restrict__ table)
@@ -224,7 +232,8 @@ __device__ __forceinline__ int butterfly(int t, int b)
 // caller offsets `buf` by c). Either way a thread's write indices are one runtime base per
 // butterfly plus compile-time offsets, and for the plain layout L divides P, so k = t mod L
 // and one set of twiddles serves all Q butterflies.
-template <class PL, int S, bool Inv, int B, int Stride, bool CtaSync, bool Mirror, bool MirrorNext>
+template <class PL, int S, bool Inv, int B, int Stride, bool CtaSync, bool Mirror, bool MirrorNext,
+          bool Derive = false>
 __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
 {
     constexpr int E = PL::E;
@@ -244,7 +253,20 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
     constexpr bool kShared = !Mirror && P % L == 0;
     constexpr int kSets = (S > 0) ? (kShared ? 1 : Q) : 1;
     float2 wt[kSets][R];
-    if constexpr (S > 0) {
+    if constexpr (S > 0 && Mirror && Derive) {
+        // Mirror pairs (L = 2P): butterfly 0 is t and reads W_{LR}^(t r) from the table;
+        // butterfly 1 is L - t, whose twiddles W_{LR}^((L - t) r) = W_R^r conj(W_{LR}^(t r)) follow
+        // with compile-time constants; for t = 0 it is P = L / 2, with twiddles W_{2R}^r.
+        static_assert(L == 2 * P, "mirror pairs take positions L - t");
+        const int k0 = t & (L - 1);
+        dft::static_for<1, R>([&](auto r_) {
+            constexpr int r = decltype(r_)::value;
+            const float2 w0 = tw[kTw + r * L + k0];
+            wt[0][r] = w0;
+            const float2 mirror = dft::mul_w<r, R, false>(make_float2(w0.x, -w0.y));
+            wt[1][r] = t == 0 ? wconst<r, 2 * R>() : mirror;
+        });
+    } else if constexpr (S > 0) {
 #pragma unroll
         for (int b = 0; b < kSets; ++b) {
             const int k = butterfly<Mirror, P>(t, b) & (L - 1);
@@ -330,15 +352,18 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
 // All passes. MirrorFirst / MirrorLast select the mirror layout of the first / last pass: the
 // registers before the first pass (the load) or after the last pass (the store) then hold
 // butterfly-mirror pairs instead of positions t + i P.
+// Derive: the mirror pass takes half its twiddles from the other half and constants (pass above)
+// instead of the table; for the computed-twiddle variants, whose tables are not correctly rounded
+// either.
 template <class PL, bool Inv, int B, int Stride = 0, bool CtaSync = false, bool MirrorFirst = false,
-          bool MirrorLast = false>
+          bool MirrorLast = false, bool Derive = false>
 __device__ __forceinline__ void run_passes(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
 {
     dft::static_for<0, PL::PASSES>([&](auto s_) {
         constexpr int S = decltype(s_)::value;
         constexpr bool kMirror = (S == 0 && MirrorFirst) || (S == PL::PASSES - 1 && MirrorLast);
         constexpr bool kMirrorNext = S + 1 == PL::PASSES - 1 && MirrorLast;
-        pass<PL, S, Inv, B, Stride, CtaSync, kMirror, kMirrorNext>(v, t, buf, tw);
+        pass<PL, S, Inv, B, Stride, CtaSync, kMirror, kMirrorNext, Derive>(v, t, buf, tw);
     });
 }
 
@@ -362,6 +387,12 @@ template <class Io, class = void>
 struct split_load : std::false_type {};
 template <class Io>
 struct split_load<Io, std::void_t<decltype(Io::kSplitLoad)>> : std::bool_constant<Io::kSplitLoad> {};
+
+// Io policies that derive part of their twiddles from constants (kDerive = true).
+template <class Io, class = void>
+struct derive_twiddles : std::false_type {};
+template <class Io>
+struct derive_twiddles<Io, std::void_t<decltype(Io::kDerive)>> : std::bool_constant<Io::kDerive> {};
 
 struct RowCtx {
     long long tf;        // this slot's transform (valid only when `active`)
@@ -432,7 +463,7 @@ __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
             if (more) {
                 io.template fetch<PL>(raw, cn);
             }
-            run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
+            run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast, derive_twiddles<Io>::value>(v, t, c.buf, tw);
             io.template store<PL, Inv>(v, c);
             if (!more) {
                 break;
@@ -458,7 +489,7 @@ __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
             if (more) {
                 io.template load<PL>(vn, cn);
             }
-            run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
+            run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast, derive_twiddles<Io>::value>(v, t, c.buf, tw);
             io.template store<PL, Inv>(v, c);
             if (!more) {
                 break;
@@ -475,7 +506,7 @@ __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
             const RowCtx c = context(tf0);
             float2 v[PL::E];
             io.template load<PL>(v, c);
-            run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
+            run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast, derive_twiddles<Io>::value>(v, t, c.buf, tw);
             io.template store<PL, Inv>(v, c);
         }
     }
@@ -596,7 +627,7 @@ __global__ void __launch_bounds__(PL::THREADS, PL::MIN_BLOCKS)
             io.template load_staged<PL>(v, c, stage + shift);
         }
         __syncthreads();  // every input read before the exchanges reuse the buffer
-        run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast>(v, t, c.buf, tw);
+        run_passes<PL, Inv, B, 0, false, Io::kMirrorFirst, Io::kMirrorLast, derive_twiddles<Io>::value>(v, t, c.buf, tw);
         io.template store<PL, Inv>(v, c);
     }
 }
@@ -971,10 +1002,14 @@ __device__ __forceinline__ void c2r_pair(int k, float2 xa, float2 xb, float2 w, 
     zmk = make_float2(ex + oy, ox - ey);
 }
 
-// Real input rows with the combine in registers (plans with SmallLast and kPairLast).
-struct R2cPairIo {
+// Real input rows with the combine in registers (plans with SmallLast and kPairLast). Derive: the
+// combine's twiddles W_{2N}^(t + r NB) = W_{2N}^t W_{2R}^r come from one table entry and
+// constants (thread 0's are all constants), and the last pass derives its mirror twiddles.
+template <bool Derive>
+struct R2cPairIoT {
     static constexpr bool kMirrorFirst = false;
     static constexpr bool kMirrorLast = true;
+    static constexpr bool kDerive = Derive;
     const float2* x;
     float2* y;
     int keep;
@@ -1002,7 +1037,28 @@ struct R2cPairIo {
         constexpr int NB = N / R;  // = 2P: positions of butterfly j are j + r NB
         float2* row = y + c.tf * keep;
         const int t = c.t;
-        if (t != 0) {
+        if constexpr (Derive) {
+            static_assert(NB == 2 * P, "half-turn twiddles W_{2N}^(t + r NB) = W_{2N}^t W_{2R}^r");
+            if (t != 0) {
+                const float2 base = c.extra[t];
+                dft::static_for<0, R>([&](auto r_) {
+                    constexpr int r = decltype(r_)::value;
+                    const float2 w = r == 0 ? base : dft::mul_w<r, 2 * R, false>(base);
+                    r2c_pair(row, N, t + r * NB, keep, v[2 * r], v[1 + 2 * (R - 1 - r)], w);
+                });
+            } else {
+                r2c_pair(row, N, 0, keep, v[0], v[0], make_float2(1.0f, 0.0f));  // X[0] and X[N]
+                dft::static_for<1, R / 2 + 1>([&](auto r_) {
+                    constexpr int r = decltype(r_)::value;
+                    r2c_pair(row, N, r * NB, keep, v[2 * r], v[2 * (R - r)], wconst<r, 2 * R>());
+                });
+                dft::static_for<0, R / 2>([&](auto r_) {
+                    constexpr int r = decltype(r_)::value;  // W_{2N}^(P + r NB) = W_{4R}^(1 + 2r)
+                    r2c_pair(row, N, P + r * NB, keep, v[1 + 2 * r], v[1 + 2 * (R - 1 - r)],
+                             wconst<1 + 2 * r, 4 * R>());
+                });
+            }
+        } else if (t != 0) {
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 const int k = t + r * NB;
@@ -1022,12 +1078,16 @@ struct R2cPairIo {
         }
     }
 };
+using R2cPairIo = R2cPairIoT<false>;
 
 // Complex rows of `keep` values to real rows with the prepare step in registers (plans with
-// kPairFirst). X[N] (the Nyquist value) is read by thread 0 alone.
-struct C2rPairIo {
+// kPairFirst). X[N] (the Nyquist value) is read by thread 0 alone. Derive: the prepare step's
+// twiddles come from one table entry and constants, as in R2cPairIoT.
+template <bool Derive>
+struct C2rPairIoT {
     static constexpr bool kMirrorFirst = true;
     static constexpr bool kMirrorLast = false;
+    static constexpr bool kDerive = Derive;
     const float2* x;
     float2* y;
     int keep;
@@ -1068,7 +1128,29 @@ struct C2rPairIo {
         const int t = c.t;
         const float2* a = raw;
         const float2* b = raw + R;
-        if (t != 0) {
+        if constexpr (Derive) {
+            static_assert(NB == 2 * P, "half-turn twiddles W_{2N}^(t + r NB) = W_{2N}^t W_{2R}^r");
+            if (t != 0) {
+                const float2 base = c.extra[t];
+                dft::static_for<0, R>([&](auto r_) {
+                    constexpr int r = decltype(r_)::value;
+                    const float2 w = r == 0 ? base : dft::mul_w<r, 2 * R, false>(base);
+                    c2r_pair(t + r * NB, a[r], b[R - 1 - r], w, v[2 * r], v[1 + 2 * (R - 1 - r)]);
+                });
+            } else {
+                float2 unused;
+                c2r_pair(0, a[0], raw[2 * R], make_float2(1.0f, 0.0f), v[0], unused);
+                dft::static_for<1, R / 2 + 1>([&](auto r_) {
+                    constexpr int r = decltype(r_)::value;
+                    c2r_pair(r * NB, a[r], a[R - r], wconst<r, 2 * R>(), v[2 * r], v[2 * (R - r)]);
+                });
+                dft::static_for<0, R / 2>([&](auto r_) {
+                    constexpr int r = decltype(r_)::value;
+                    c2r_pair(P + r * NB, b[r], b[R - 1 - r], wconst<1 + 2 * r, 4 * R>(), v[1 + 2 * r],
+                             v[1 + 2 * (R - 1 - r)]);
+                });
+            }
+        } else if (t != 0) {
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 const int k = t + r * NB;
@@ -1148,5 +1230,6 @@ struct C2rPairIo {
         C2rIo{x, y, keep, scale}.template store<PL, Inv>(v, c);
     }
 };
+using C2rPairIo = C2rPairIoT<false>;
 
 }  // namespace spectral::engine

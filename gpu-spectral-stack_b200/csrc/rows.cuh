@@ -214,7 +214,8 @@ struct RowEngine {
 
     // `batch` real rows of n points (2 <= n <= 8192) to rows of `keep` (1 .. n/2 + 1) outputs.
     // Where the plan with the small radix last leaves two butterflies per thread in the last
-    // pass, the combine runs in registers on mirror pairs (R2cPairIo).
+    // pass, the combine runs in registers on mirror pairs (R2cPairIoT); the computed-twiddle
+    // variants derive the mirror and combine twiddles from constants, the table variant reads them.
     static void r2c(const float* x, float2* y, int n, long long batch, int keep, float2* /*work*/,
                     cudaStream_t s)
     {
@@ -225,7 +226,7 @@ struct RowEngine {
             const auto* xz = reinterpret_cast<const float2*>(x);
             using PP = RowPlan<RowKind::R2c, M, true>;
             if constexpr (M >= 32 && PP::kPairLast) {
-                launch_rows<PP, false, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(R2cPairIo{xz, y, keep}, batch, s, w);
+                launch_rows<PP, false, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(R2cPairIoT<!Table>{xz, y, keep}, batch, s, w);
             } else {
                 using PL = RowPlan<RowKind::R2c, M>;
                 launch_rows<PL, false, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(R2cIo{xz, y, keep}, batch, s, w);
@@ -246,7 +247,7 @@ struct RowEngine {
             const float2* w = row_half_turn<M, Table, rc.smem_twiddles>();
             auto* yz = reinterpret_cast<float2*>(y);
             if constexpr (M >= 32 && PL::kPairFirst) {
-                launch_rows<PL, true, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(C2rPairIo{x, yz, keep, 1.0f / M}, batch, s, w);
+                launch_rows<PL, true, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(C2rPairIoT<!Table>{x, yz, keep, 1.0f / M}, batch, s, w);
             } else {
                 launch_rows<PL, true, B, Table, rc.smem_twiddles, rc.persistent>(C2rIo{x, yz, keep, 1.0f / M}, batch, s, w);
             }

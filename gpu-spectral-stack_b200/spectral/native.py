@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_ipc_close": (_i, [_p]),
     "spectral_ipc_free": (_i, [_p]),
     "spectral_mode_contract": (_i, [_p, _p, _p, _ll, _i, _i, _ll, _p]),
+    "spectral_mode_contract_method": (_i, [_p, _p, _p, _ll, _i, _i, _ll, _i, _p]),
     "spectral_fp32_ceiling": (_i, [_p, _i, _i, _p, ctypes.POINTER(ctypes.c_double)]),
     "spectral_spectrum": (_i, [_s, _p, _p, _p, _ll, _i, _ll, _p]),
     "spectral_fir": (_i, [_s, _p, _p, _p, _ll, _i, _i, _ll, _p]),

@@ -264,6 +264,19 @@ SPECTRAL_API int spectral_ipc_free(void* ptr);
 SPECTRAL_API int spectral_mode_contract(const void* x, const void* w, void* out, long long batch, int cin,
                            int cout, long long modes, void* stream);
 
+/* The same contraction with the method chosen by the caller (no reference counterpart):
+ *   SPECTRAL_CONTRACT_AUTO    what spectral_mode_contract uses;
+ *   SPECTRAL_CONTRACT_FP32    FP32 fused multiply-adds on the CUDA cores;
+ *   SPECTRAL_CONTRACT_TENSOR  the tcgen05 tensor cores with every FP32 operand split into two TF32
+ *                             parts (three products per multiply: FP32-level error). Needs batch
+ *                             and cout multiples of 64, cin of 8, modes of 4, 16-byte aligned
+ *                             arrays; other shapes are refused. */
+#define SPECTRAL_CONTRACT_AUTO 0
+#define SPECTRAL_CONTRACT_FP32 1
+#define SPECTRAL_CONTRACT_TENSOR 2
+SPECTRAL_API int spectral_mode_contract_method(const void* x, const void* w, void* out, long long batch,
+                                               int cin, int cout, long long modes, int method, void* stream);
+
 /* The FP32 arithmetic ceiling, for the roofline of FP32-bound kernels such as the contraction
  * (reference: csrc/tools/peaks.cu:46-70, a separate tool there). Launches one full wave of CTAs
  * that run independent fused multiply-add chains and nothing else: scalar FFMA (packed == 0) or

@@ -233,7 +233,7 @@ __device__ __forceinline__ int butterfly(int t, int b)
 // butterfly plus compile-time offsets, and for the plain layout L divides P, so k = t mod L
 // and one set of twiddles serves all Q butterflies.
 template <class PL, int S, bool Inv, int B, int Stride, bool CtaSync, bool Mirror, bool MirrorNext,
-          bool Derive = false>
+          int Derive = 0>
 __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
 {
     constexpr int E = PL::E;
@@ -253,7 +253,26 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
     constexpr bool kShared = !Mirror && P % L == 0;
     constexpr int kSets = (S > 0) ? (kShared ? 1 : Q) : 1;
     float2 wt[kSets][R];
-    if constexpr (S > 0 && Mirror && Derive) {
+    // Radix-16 passes whose twiddles are derived (Derive >= 3, or >= 2 where the table spans 32
+    // or more entries per r, i.e. 256-byte loads per warp).
+    constexpr bool kDerive16 = !Mirror && kShared && R == 16 && (Derive >= 3 || (Derive >= 2 && L >= 32));
+    if constexpr (S > 0 && kDerive16) {
+        // W^(k r) for r = r0 + 4 r1: the table's r in {1, 2, 3} and {4, 8, 12}, and one complex
+        // product W^(k r0) W^(4 k r1) for each of the other nine (at most two roundings).
+        const int k = t & (L - 1);
+        dft::static_for<1, 4>([&](auto r_) {
+            constexpr int r = decltype(r_)::value;
+            wt[0][r] = tw[kTw + r * L + k];
+            wt[0][4 * r] = tw[kTw + 4 * r * L + k];
+        });
+        dft::static_for<1, 4>([&](auto r1_) {
+            constexpr int r1 = decltype(r1_)::value;
+            dft::static_for<1, 4>([&](auto r0_) {
+                constexpr int r0 = decltype(r0_)::value;
+                wt[0][r0 + 4 * r1] = cmul(wt[0][r0], wt[0][4 * r1]);
+            });
+        });
+    } else if constexpr (S > 0 && Mirror && Derive >= 1) {
         // Mirror pairs (L = 2P): butterfly 0 is t and reads W_{LR}^(t r) from the table;
         // butterfly 1 is L - t, whose twiddles W_{LR}^((L - t) r) = W_R^r conj(W_{LR}^(t r)) follow
         // with compile-time constants; for t = 0 it is P = L / 2, with twiddles W_{2R}^r.
@@ -352,11 +371,12 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
 // All passes. MirrorFirst / MirrorLast select the mirror layout of the first / last pass: the
 // registers before the first pass (the load) or after the last pass (the store) then hold
 // butterfly-mirror pairs instead of positions t + i P.
-// Derive: the mirror pass takes half its twiddles from the other half and constants (pass above)
-// instead of the table; for the computed-twiddle variants, whose tables are not correctly rounded
-// either.
+// Derive: 1, the mirror pass takes half its twiddles from the other half and constants (pass
+// above) instead of the table; 2 and 3, radix-16 passes also form 9 of their 15 twiddles from
+// the other 6 (see pass). For the computed-twiddle variants, whose tables are not correctly
+// rounded either.
 template <class PL, bool Inv, int B, int Stride = 0, bool CtaSync = false, bool MirrorFirst = false,
-          bool MirrorLast = false, bool Derive = false>
+          bool MirrorLast = false, int Derive = 0>
 __device__ __forceinline__ void run_passes(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
 {
     dft::static_for<0, PL::PASSES>([&](auto s_) {
@@ -388,11 +408,11 @@ struct split_load : std::false_type {};
 template <class Io>
 struct split_load<Io, std::void_t<decltype(Io::kSplitLoad)>> : std::bool_constant<Io::kSplitLoad> {};
 
-// Io policies that derive part of their twiddles from constants (kDerive = true).
+// Io policies that derive part of their twiddles (kDerive > 0; the level run_passes takes).
 template <class Io, class = void>
-struct derive_twiddles : std::false_type {};
+struct derive_twiddles : std::integral_constant<int, 0> {};
 template <class Io>
-struct derive_twiddles<Io, std::void_t<decltype(Io::kDerive)>> : std::bool_constant<Io::kDerive> {};
+struct derive_twiddles<Io, std::void_t<decltype(Io::kDerive)>> : std::integral_constant<int, Io::kDerive> {};
 
 struct RowCtx {
     long long tf;        // this slot's transform (valid only when `active`)
@@ -985,17 +1005,20 @@ __device__ __forceinline__ void r2c_pair(float2* row, int n, int k, int keep, fl
     }
 }
 
-// Z[k] and Z[N - k] from xa = X[k], xb = X[N - k], w = W_{2N}^k.
-__device__ __forceinline__ void c2r_pair(int k, float2 xa, float2 xb, float2 w, float2& zk, float2& zmk)
+// Z[k] and Z[N - k] from xa = X[k], xb = X[N - k], w = W_{2N}^k, times 2 `half` (half = 1/2 gives
+// the prepare step itself; the inverse's 1 / N folded in gives half = 1 / (2N), a power of two, so
+// the results are the same bits as scaling the outputs afterwards).
+__device__ __forceinline__ void c2r_pair(int k, float2 xa, float2 xb, float2 w, float2& zk, float2& zmk,
+                                         float half = 0.5f)
 {
     if (k == 0) {
         xa.y = 0.0f;
         xb.y = 0.0f;
     }
-    const float ex = 0.5f * (xa.x + xb.x);
-    const float ey = 0.5f * (xa.y - xb.y);
-    const float dx = 0.5f * (xa.x - xb.x);
-    const float dy = 0.5f * (xa.y + xb.y);
+    const float ex = half * (xa.x + xb.x);
+    const float ey = half * (xa.y - xb.y);
+    const float dx = half * (xa.x - xb.x);
+    const float dy = half * (xa.y + xb.y);
     const float ox = fmaf(dx, w.x, dy * w.y);
     const float oy = fmaf(dy, w.x, -(dx * w.y));
     zk = make_float2(ex - oy, ey + ox);
@@ -1005,11 +1028,11 @@ __device__ __forceinline__ void c2r_pair(int k, float2 xa, float2 xb, float2 w, 
 // Real input rows with the combine in registers (plans with SmallLast and kPairLast). Derive: the
 // combine's twiddles W_{2N}^(t + r NB) = W_{2N}^t W_{2R}^r come from one table entry and
 // constants (thread 0's are all constants), and the last pass derives its mirror twiddles.
-template <bool Derive>
+template <int Derive>
 struct R2cPairIoT {
     static constexpr bool kMirrorFirst = false;
     static constexpr bool kMirrorLast = true;
-    static constexpr bool kDerive = Derive;
+    static constexpr int kDerive = Derive;
     const float2* x;
     float2* y;
     int keep;
@@ -1037,7 +1060,7 @@ struct R2cPairIoT {
         constexpr int NB = N / R;  // = 2P: positions of butterfly j are j + r NB
         float2* row = y + c.tf * keep;
         const int t = c.t;
-        if constexpr (Derive) {
+        if constexpr (Derive >= 1) {
             static_assert(NB == 2 * P, "half-turn twiddles W_{2N}^(t + r NB) = W_{2N}^t W_{2R}^r");
             if (t != 0) {
                 const float2 base = c.extra[t];
@@ -1078,16 +1101,16 @@ struct R2cPairIoT {
         }
     }
 };
-using R2cPairIo = R2cPairIoT<false>;
+using R2cPairIo = R2cPairIoT<0>;
 
 // Complex rows of `keep` values to real rows with the prepare step in registers (plans with
 // kPairFirst). X[N] (the Nyquist value) is read by thread 0 alone. Derive: the prepare step's
 // twiddles come from one table entry and constants, as in R2cPairIoT.
-template <bool Derive>
+template <int Derive>
 struct C2rPairIoT {
     static constexpr bool kMirrorFirst = true;
     static constexpr bool kMirrorLast = false;
-    static constexpr bool kDerive = Derive;
+    static constexpr int kDerive = Derive;
     const float2* x;
     float2* y;
     int keep;
@@ -1126,47 +1149,48 @@ struct C2rPairIoT {
         constexpr int R = PL::radix(0);
         constexpr int NB = N / R;  // = 2P
         const int t = c.t;
+        const float half = 0.5f * scale;  // the 1 / N of the inverse, folded in exactly
         const float2* a = raw;
         const float2* b = raw + R;
-        if constexpr (Derive) {
+        if constexpr (Derive >= 1) {
             static_assert(NB == 2 * P, "half-turn twiddles W_{2N}^(t + r NB) = W_{2N}^t W_{2R}^r");
             if (t != 0) {
                 const float2 base = c.extra[t];
                 dft::static_for<0, R>([&](auto r_) {
                     constexpr int r = decltype(r_)::value;
                     const float2 w = r == 0 ? base : dft::mul_w<r, 2 * R, false>(base);
-                    c2r_pair(t + r * NB, a[r], b[R - 1 - r], w, v[2 * r], v[1 + 2 * (R - 1 - r)]);
+                    c2r_pair(t + r * NB, a[r], b[R - 1 - r], w, v[2 * r], v[1 + 2 * (R - 1 - r)], half);
                 });
             } else {
                 float2 unused;
-                c2r_pair(0, a[0], raw[2 * R], make_float2(1.0f, 0.0f), v[0], unused);
+                c2r_pair(0, a[0], raw[2 * R], make_float2(1.0f, 0.0f), v[0], unused, half);
                 dft::static_for<1, R / 2 + 1>([&](auto r_) {
                     constexpr int r = decltype(r_)::value;
-                    c2r_pair(r * NB, a[r], a[R - r], wconst<r, 2 * R>(), v[2 * r], v[2 * (R - r)]);
+                    c2r_pair(r * NB, a[r], a[R - r], wconst<r, 2 * R>(), v[2 * r], v[2 * (R - r)], half);
                 });
                 dft::static_for<0, R / 2>([&](auto r_) {
                     constexpr int r = decltype(r_)::value;
                     c2r_pair(P + r * NB, b[r], b[R - 1 - r], wconst<1 + 2 * r, 4 * R>(), v[1 + 2 * r],
-                             v[1 + 2 * (R - 1 - r)]);
+                             v[1 + 2 * (R - 1 - r)], half);
                 });
             }
         } else if (t != 0) {
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 const int k = t + r * NB;
-                c2r_pair(k, a[r], b[R - 1 - r], c.extra[k], v[2 * r], v[1 + 2 * (R - 1 - r)]);
+                c2r_pair(k, a[r], b[R - 1 - r], c.extra[k], v[2 * r], v[1 + 2 * (R - 1 - r)], half);
             }
         } else {
             float2 unused;
-            c2r_pair(0, a[0], raw[2 * R], c.extra[0], v[0], unused);
+            c2r_pair(0, a[0], raw[2 * R], c.extra[0], v[0], unused, half);
 #pragma unroll
             for (int r = 1; r <= R / 2; ++r) {
-                c2r_pair(r * NB, a[r], a[R - r], c.extra[r * NB], v[2 * r], v[2 * (R - r)]);
+                c2r_pair(r * NB, a[r], a[R - r], c.extra[r * NB], v[2 * r], v[2 * (R - r)], half);
             }
 #pragma unroll
             for (int r = 0; r < R / 2; ++r) {
                 c2r_pair(P + r * NB, b[r], b[R - 1 - r], c.extra[P + r * NB], v[1 + 2 * r],
-                         v[1 + 2 * (R - 1 - r)]);
+                         v[1 + 2 * (R - 1 - r)], half);
             }
         }
     }
@@ -1224,12 +1248,20 @@ struct C2rPairIoT {
         prepare<PL>(v, c, [&](int k) { return k < kp ? __ldg(row + k) : zero; });
     }
 
+    // The 1 / N scale was applied in the prepare step (combine).
     template <class PL, bool Inv>
     __device__ __forceinline__ void store(float2 (&v)[PL::E], const RowCtx& c) const
     {
-        C2rIo{x, y, keep, scale}.template store<PL, Inv>(v, c);
+        if (!c.active) {
+            return;
+        }
+        float2* row = y + c.tf * PL::N + c.t;
+#pragma unroll
+        for (int i = 0; i < PL::E; ++i) {
+            row[i * PL::P] = v[i];
+        }
     }
 };
-using C2rPairIo = C2rPairIoT<false>;
+using C2rPairIo = C2rPairIoT<0>;
 
 }  // namespace spectral::engine

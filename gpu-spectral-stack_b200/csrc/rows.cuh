@@ -161,6 +161,10 @@ void launch_rows_staged(const Io& io, long long batch, cudaStream_t stream, cons
     launch_pdl(kernel, grid, static_cast<unsigned>(PL::THREADS), smem, stream, io, batch, tw, extra_table, device_fault_word());
 }
 
+// How much of their twiddles the computed-twiddle variants' real-row kernels derive instead of
+// loading (engine.cuh: run_passes' Derive).
+constexpr int kDeriveLevel = 1;
+
 // Calls f(std::integral_constant<int, n>) for a power of two n in [Lo, Hi], else throws.
 template <int Lo, int Hi, class F>
 void dispatch_pow2(int n, F&& f)
@@ -226,7 +230,7 @@ struct RowEngine {
             const auto* xz = reinterpret_cast<const float2*>(x);
             using PP = RowPlan<RowKind::R2c, M, true>;
             if constexpr (M >= 32 && PP::kPairLast) {
-                launch_rows<PP, false, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(R2cPairIoT<!Table>{xz, y, keep}, batch, s, w);
+                launch_rows<PP, false, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(R2cPairIoT<Table ? 0 : kDeriveLevel>{xz, y, keep}, batch, s, w);
             } else {
                 using PL = RowPlan<RowKind::R2c, M>;
                 launch_rows<PL, false, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(R2cIo{xz, y, keep}, batch, s, w);
@@ -247,7 +251,7 @@ struct RowEngine {
             const float2* w = row_half_turn<M, Table, rc.smem_twiddles>();
             auto* yz = reinterpret_cast<float2*>(y);
             if constexpr (M >= 32 && PL::kPairFirst) {
-                launch_rows<PL, true, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(C2rPairIoT<!Table>{x, yz, keep, 1.0f / M}, batch, s, w);
+                launch_rows<PL, true, B, Table, rc.smem_twiddles, rc.persistent, rc.prefetch>(C2rPairIoT<Table ? 0 : kDeriveLevel>{x, yz, keep, 1.0f / M}, batch, s, w);
             } else {
                 launch_rows<PL, true, B, Table, rc.smem_twiddles, rc.persistent>(C2rIo{x, yz, keep, 1.0f / M}, batch, s, w);
             }

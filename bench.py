@@ -1368,7 +1368,15 @@ def run_sweep(args) -> None:
     gen = torch.Generator(device="cuda").manual_seed(0)
     sets = [(torch.randn(SWEEP_POINTS, dtype=torch.complex64, device="cuda", generator=gen),
              torch.empty(SWEEP_POINTS + 4096, dtype=torch.complex64, device="cuda")) for _ in range(SETS)]
-    work = torch.empty(2 * SWEEP_POINTS + 4096, dtype=torch.complex64, device="cuda")
+    work_holder = [torch.empty(1, dtype=torch.complex64, device="cuda")]
+
+    def work_for(fn: str, *args) -> int:
+        """A workspace of at least the size the library reports for this call (spectral_*_workspace):
+        the library can check only that the pointer is not null, not the buffer's length."""
+        need = native.workspace(fn, *args)
+        if work_holder[0].numel() < need:
+            work_holder[0] = torch.empty(need, dtype=torch.complex64, device="cuda")
+        return work_holder[0].data_ptr()
     impls = [n for n in spectral.FFT_IMPLS]
     sizes = [1 << k for k in range(1, 13)]
     results = []
@@ -1409,33 +1417,36 @@ def run_sweep(args) -> None:
                 elif op in ("fft_r2c", "fft_c2r") and n <= max_real:
                     b = SWEEP_POINTS // n
                     fn = "spectral_r2c" if op == "fft_r2c" else "spectral_c2r"
+                    wp = work_for("spectral_real_workspace", imp, n, b)
                     timed(op, impl, n, b, bm.fft_real_work(n, b),
-                          lambda x, y, n=n, b=b, fn=fn: native.call(fn, imp, x, y, n, b, work.data_ptr(), stream))
+                          lambda x, y, n=n, b=b, fn=fn, wp=wp: native.call(fn, imp, x, y, n, b, wp, stream))
                 elif op.startswith("fft2_") and n <= max_n and n * n <= SWEEP_POINTS:
                     b = SWEEP_POINTS // (n * n)
                     for method, cname in ((1, "strided"), (0, "transpose")):
                         if method == 1 and not has_columns:
                             continue
                         name = f"{impl}/{cname}"
+                        wp = work_for(f"spectral_{op}_workspace", imp, method, n, n, b)
                         if op == "fft2_c2c":
                             fb = bm.fft_c2c_work(n * n, b)
-                            call = lambda x, y, n=n, b=b, m=method: native.call(
-                                "spectral_fft2_c2c", imp, m, x, y, n, n, b, 0, work.data_ptr(), stream)
+                            call = lambda x, y, n=n, b=b, m=method, wp=wp: native.call(
+                                "spectral_fft2_c2c", imp, m, x, y, n, n, b, 0, wp, stream)
                         elif op == "fft2_r2c":
                             fb = bm.fft2_real_work(n, n, b)
-                            call = lambda x, y, n=n, b=b, m=method: native.call(
-                                "spectral_fft2_r2c", imp, m, x, y, n, n, b, work.data_ptr(), stream)
+                            call = lambda x, y, n=n, b=b, m=method, wp=wp: native.call(
+                                "spectral_fft2_r2c", imp, m, x, y, n, n, b, wp, stream)
                         else:
                             fb = bm.fft2_real_work(n, n, b)
-                            call = lambda x, y, n=n, b=b, m=method: native.call(
-                                "spectral_fft2_c2r", imp, m, x, y, n, n, b, work.data_ptr(), stream)
+                            call = lambda x, y, n=n, b=b, m=method, wp=wp: native.call(
+                                "spectral_fft2_c2r", imp, m, x, y, n, n, b, wp, stream)
                         timed(op, name, n, b, fb, call)
                 elif op in ("rfft2_modes", "irfft2_modes") and 2 <= n <= max_n and n * n <= SWEEP_POINTS:
                     b = SWEEP_POINTS // (n * n)
                     m = max(1, n // 8)
                     fn = "spectral_rfft2_modes" if op == "rfft2_modes" else "spectral_irfft2_modes"
+                    wp = work_for(f"{fn}_workspace", imp, n, n, m, m, b)
                     timed(op, impl, n, b, bm.pruned_work(n, n, m, m, b),
-                          lambda x, y, n=n, b=b, m=m, fn=fn: native.call(fn, imp, x, y, n, n, m, m, b, work.data_ptr(), stream))
+                          lambda x, y, n=n, b=b, m=m, fn=fn, wp=wp: native.call(fn, imp, x, y, n, n, m, m, b, wp, stream))
     prop = torch.cuda.get_device_properties(0)
     comments = [f"device: {prop.name}, {prop.multi_processor_count} SMs",
                 f"torch {torch.__version__}, CUDA {torch.version.cuda}",

@@ -27,8 +27,10 @@
 // W >= 16, a half-warp's 16 consecutive positions are never split by a pad entry (with W = 8, as
 // for a radix-8 first pass, they would straddle one and wrap onto a bank already in use). Where
 // a transform has fewer than 16 threads, W = L R keeps each transform's writes spread so that
-// the transforms sharing a half-warp (slots P apart in banks) do not collide. The reference's
-// stage store has 4.5 M bank conflicts per 2^24 points (docs/PROFILING.md:129-136).
+// the transforms sharing a half-warp (slots P apart in banks) do not collide. One exchange is
+// permuted instead of padded: the one after a mirror first pass of radix below 16 (see pass).
+// The reference's stage store has 4.5 M bank conflicts per 2^24 points
+// (docs/PROFILING.md:129-136).
 //
 // Twiddles: one table per pass after the first, in shared memory or read from global memory
 // (rows.cuh chooses per size): entry r L + k of pass s holds W_{L R}^(k r) = exp(-2 pi i k r /
@@ -243,8 +245,15 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
     constexpr int Q = E / R;  // butterflies per thread
     constexpr bool kLast = S == PL::PASSES - 1;
     constexpr int kTw = PL::tw_offset(S);
-    constexpr bool kPad = Stride == 0 && L < 16;
     constexpr int W = PL::pad_group(S);  // positions per pad entry (a multiple of L R)
+    // A mirror first pass of radix R < 16 (the inverse real rows): butterfly 1 of thread t is
+    // j = 2 P - t, so a half-warp's 16 butterflies start at an odd j, and with one pad entry per
+    // 16 positions its first and last write share a bank pair (a 2-way conflict on every write).
+    // This exchange instead permutes each aligned block of 16 positions: position q is stored at
+    // q ^ ((q / 16) mod R), which gives any 16 consecutive butterflies distinct bank pairs for
+    // each r and keeps a half-warp's 16 consecutive reads inside one block.
+    constexpr bool kSwizzle = Stride == 0 && Mirror && !kLast && S == 0 && L == 1 && W == 16 && R < 16;
+    constexpr bool kPad = Stride == 0 && L < 16 && !kSwizzle;
     static_assert(!Mirror || Q == 2, "mirror pairing needs two butterflies per thread");
     static_assert(Mirror || kLast || P % L == 0, "the plain exchange layout needs L to divide P");
 
@@ -320,9 +329,10 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
             // The R outputs span L R consecutive positions inside one group of W.
             const int pos0 = (j - k) * R + k;
             const int base = kPad ? pos0 + L * (pos0 / W) : pos0;
+            const int key = kSwizzle ? (pos0 >> 4) & (R - 1) : 0;  // pos0 = R j: low bits free
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                const int idx = base + r * L;
+                const int idx = kSwizzle ? base + (r ^ key) : base + r * L;
                 buf[Stride == 0 ? idx : idx * Stride] = u[r];
             }
         }
@@ -340,9 +350,22 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
 #pragma unroll
                 for (int r = 0; r < R2; ++r) {
                     const int q = j + r * NB2;
-                    const int idx = kPad ? q + L * (q / W) : q;
+                    const int idx = kSwizzle ? q ^ ((q >> 4) & (R - 1)) : kPad ? q + L * (q / W) : q;
                     v[b + r * Q2] = buf[Stride == 0 ? idx : idx * Stride];
                 }
+            }
+        } else if constexpr (kSwizzle && (P / 16) % R == 0) {
+            // (t + i P) / 16 = t / 16 + i P / 16 with i P / 16 a multiple of R: one key for all i.
+            const int base = t ^ ((t >> 4) & (R - 1));
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                v[i] = buf[base + i * P];
+            }
+        } else if constexpr (kSwizzle) {
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                const int q = t + i * P;
+                v[i] = buf[q ^ ((q >> 4) & (R - 1))];
             }
         } else if constexpr (kPad && P % W == 0) {
             // pad(t + i P) = t + L floor(t / W) + i (P + L P / W), since W divides P.

@@ -53,3 +53,23 @@ def test_wrong_dtype_is_rejected():
     x = torch.zeros(4, dtype=torch.float32, device="cuda")
     with pytest.raises(RuntimeError, match="complex64"):
         spectral.scale(x, 0.5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("offset", [0, 1])
+@pytest.mark.parametrize("n", [2, 3, 4097, 1 << 22])
+def test_scale_on_both_paths_and_in_place(offset, n):
+    # offset 0: 16-byte aligned (two values per access, an odd tail on its own); offset 1: 8 bytes
+    # off (the one-value kernel). In place through the C ABI too: every value is read before the
+    # same thread writes it.
+    from spectral import native
+
+    g = torch.Generator(device="cuda").manual_seed(n + offset)
+    base = torch.randn(n + 1, dtype=torch.complex64, device="cuda", generator=g)
+    x = base[offset:offset + n]
+    expected = x * 0.25
+    torch.testing.assert_close(spectral.scale(x, 0.25), expected, rtol=0, atol=0)
+    stream = torch.cuda.current_stream().cuda_stream
+    native.call("spectral_scale", x.data_ptr(), x.data_ptr(), n, 0.25, stream)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(x, expected, rtol=0, atol=0)

@@ -20,7 +20,9 @@ scaling, batch sharding with no communication); a barrier and a synchronize brac
 steps, and the slowest rank's time counts.
 
 Also on the line: `roofline` (the dominant kernel's achieved bytes / its average CUDA-event
-duration against the measured HBM copy peak), `e2e` (the same metric through the public torch
+duration against the measured HBM copy peak, and against a copy of the same size measured in the
+run, `size_matched_copy`: a 4 GB copy reaches the peak, a copy of one launch's bytes does not),
+`e2e` (the same metric through the public torch
 API with host buffers: pinned host -> device, both transforms, device -> host, every step),
 `cpu_baseline` (the float64 oracle, numpy's pocketfft as in the reference's CPU path, on the
 host's cores), `clocks` (SM clock and throttle reasons, sampled through NVML during the timed steps) and `gpu_launches`.
@@ -947,6 +949,31 @@ def ncu_traffic(kernel: str, workload: str) -> float | None:
     return None
 
 
+def size_matched_copy(nbytes: int, stream) -> float:
+    """GB/s of a plain device-to-device copy (torch copy_) whose read + write traffic is `nbytes`,
+    the dominant kernel's algorithmic bytes per launch: 4 rotating buffer pairs, 20 back-to-back
+    copies per round, the median of 7 rounds after 6 warm-up copies. Copy bandwidth grows with
+    the size of the copy (the measured peak is a 4 GB copy), so this is the ceiling for a kernel
+    that moves this many bytes per launch."""
+    import torch
+
+    n = max(1, nbytes // 8)  # float32 elements per buffer: n * 4 bytes read and written
+    pairs = [(torch.empty(n, device="cuda").fill_(1.0), torch.empty(n, device="cuda")) for _ in range(4)]
+    with torch.cuda.stream(stream):
+        for k in range(6):
+            pairs[k % 4][1].copy_(pairs[k % 4][0])
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+        ev[0].record(stream)
+        for r in range(7):
+            for k in range(20):
+                pairs[k % 4][1].copy_(pairs[k % 4][0])
+            ev[r + 1].record(stream)
+    ev[-1].synchronize()
+    ms = statistics.median(a.elapsed_time(b) / 20 for a, b in zip(ev, ev[1:]))
+    del pairs
+    return 8 * n / (ms * 1e-3) / 1e9
+
+
 def fp32_ceiling(native, stream) -> float:
     """The GPU's FP32 ceiling in TFLOP/s: the faster of the scalar-FFMA and packed-FFMA2 forms of
     spectral_fp32_ceiling, each the median of 5 timed launches after 2 warm-up launches."""
@@ -1233,6 +1260,11 @@ def run_ours(args) -> None:
                 "per_kernel_in_step_us": {n: round(1000 * ms, 2) for (n, _), ms in zip(kernels, in_step_ms)},
                 "per_kernel_us": {n: round(1000 * ms, 2) for (n, _), ms in zip(kernels, per_kernel_ms)},
                 "per_kernel_note": "per_kernel_us: each launch bracketed by its own events (a separate pass)"}
+    copy_gbs = size_matched_copy(dom_bytes, stream)
+    roofline["size_matched_copy"] = {
+        "gbs": round(copy_gbs, 1), "frac": round(achieved / copy_gbs, 4),
+        "how": "torch copy_ moving the dominant kernel's bytes per launch (read + write), 4 rotating "
+               "buffer pairs, median of 7 rounds of 20 back-to-back copies; measured in this run"}
 
     # End to end through the public torch API: host -> device, the step, device -> host.
     e2e = None

@@ -61,11 +61,30 @@ def test_irfft2_matches_the_oracle(rng, impl, columns, n1, n2):
 
 
 @pytest.mark.parametrize(("impl", "columns"), METHODS, ids=METHOD_IDS)
-def test_irfft2_of_a_non_hermitian_spectrum_matches_torch(rng, impl, columns):
-    spectrum = random_complex(rng, (2, 16, 9))
-    expected = torch.fft.irfft2(torch.from_numpy(spectrum).to(torch.complex128), s=(16, 16))
-    y = spectral.irfft2(cuda(spectrum), 16, impl=impl, columns=columns)
-    assert_transform_close(y, expected.numpy(), 256, axes=AXES)
+@pytest.mark.parametrize("n", [16, 256])
+def test_irfft2_of_a_non_hermitian_spectrum_matches_torch(rng, impl, columns, n):
+    # Columns 0 and n/2 with arbitrary imaginary parts: only their real parts after the column
+    # transforms reach the output, as in numpy and torch.
+    spectrum = random_complex(rng, (2, n, n // 2 + 1))
+    expected = torch.fft.irfft2(torch.from_numpy(spectrum).to(torch.complex128), s=(n, n))
+    y = spectral.irfft2(cuda(spectrum), n, impl=impl, columns=columns)
+    assert_transform_close(y, expected.numpy(), n * n, axes=AXES)
+
+
+@pytest.mark.parametrize("impl", ENGINES)
+@pytest.mark.parametrize("fields", [1, 2, 75, 150, 301])
+def test_many_256_x_256_fields(rng, impl, fields):
+    # Field counts below, at and above one per SM pair and per SM (74 and 148 on a B200), so the
+    # persistent row and column grids walk several tiles; the oracle checks the first, middle
+    # and last fields.
+    n = 256
+    x = random_real(rng, (fields, n, n))
+    s = spectral.rfft2(cuda(x), impl=impl, columns="strided")
+    y = spectral.irfft2(s, n, impl=impl, columns="strided")
+    idx = sorted({0, fields // 2, fields - 1})
+    assert_transform_close(s[idx], ref.rfft2(x[idx]), n * n, axes=AXES)
+    spectrum = s[idx].cpu().numpy()
+    assert_transform_close(y[idx], ref.irfft2(spectrum, (n, n)), n * n, axes=AXES)
 
 
 @pytest.mark.parametrize(("impl", "columns"), METHODS, ids=METHOD_IDS)

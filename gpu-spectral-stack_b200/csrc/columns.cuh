@@ -36,7 +36,9 @@ struct ColumnCtx {
     float2* tile;
 };
 
-template <class PL, int C, bool Inv, int B, bool Table, class Io, bool TwGlobal = false>
+// Prefetch: the next tile's loads are issued before this tile's passes (the Io's load must not
+// read what another tile stores: true of column tiles, which are disjoint sets of columns).
+template <class PL, int C, bool Inv, int B, bool Table, class Io, bool TwGlobal = false, bool Prefetch = false>
 __global__ void __launch_bounds__(C * PL::P, PL::MIN_BLOCKS)
     column_kernel(const Io io, long long transforms, const float2* __restrict__ tw_table)
 {
@@ -55,8 +57,7 @@ __global__ void __launch_bounds__(C * PL::P, PL::MIN_BLOCKS)
 
     const int c = threadIdx.x % C;
     const int t = threadIdx.x / C;
-    for (long long f0 = static_cast<long long>(blockIdx.x) * C; f0 < transforms;
-         f0 += static_cast<long long>(gridDim.x) * C) {
+    auto context = [&](long long f0) {
         ColumnCtx ctx;
         ctx.f0 = f0;
         ctx.f = f0 + c;
@@ -65,10 +66,31 @@ __global__ void __launch_bounds__(C * PL::P, PL::MIN_BLOCKS)
         ctx.c = c;
         ctx.t = t;
         ctx.tile = tile;
-        float2 v[PL::E];
-        io.template load<PL>(v, ctx);
-        run_passes<PL, Inv, B, C, true>(v, t, tile + c, tw);
-        io.template store<PL, C, Inv>(v, ctx);
+        return ctx;
+    };
+    const long long stride = static_cast<long long>(gridDim.x) * C;
+    if constexpr (Prefetch) {
+        float2 next[PL::E];
+        io.template load<PL>(next, context(static_cast<long long>(blockIdx.x) * C));
+        for (long long f0 = static_cast<long long>(blockIdx.x) * C; f0 < transforms; f0 += stride) {
+            const ColumnCtx ctx = context(f0);
+            float2 v[PL::E];
+#pragma unroll
+            for (int i = 0; i < PL::E; ++i) {
+                v[i] = next[i];
+            }
+            io.template load<PL>(next, context(f0 + stride));  // inactive past the end: zeros
+            run_passes<PL, Inv, B, C, true>(v, t, tile + c, tw);
+            io.template store<PL, C, Inv>(v, ctx);
+        }
+    } else {
+        for (long long f0 = static_cast<long long>(blockIdx.x) * C; f0 < transforms; f0 += stride) {
+            const ColumnCtx ctx = context(f0);
+            float2 v[PL::E];
+            io.template load<PL>(v, ctx);
+            run_passes<PL, Inv, B, C, true>(v, t, tile + c, tw);
+            io.template store<PL, C, Inv>(v, ctx);
+        }
     }
 }
 
@@ -80,6 +102,15 @@ constexpr std::size_t column_smem_bytes()
               + static_cast<std::size_t>(C) * (PL::N + 1));
 }
 
+// Io policies whose load may run one tile ahead (kPrefetch = true): their loads never read what
+// another tile's store writes. The prefetch pays for 64- to 512-point columns (measured on B200,
+// 2^24 points per call: 256 points 29.2 -> 27.2 µs, 512 points 37.1 -> 29.8 µs, 128 points
+// 26.9 -> 25.6 µs, 64 points 29.7 -> 27.1 µs); elsewhere it is untested and off.
+template <class Io, class = void>
+struct column_prefetch : std::false_type {};
+template <class Io>
+struct column_prefetch<Io, std::void_t<decltype(Io::kPrefetch)>> : std::bool_constant<Io::kPrefetch> {};
+
 template <class PL, bool Inv, int B, bool Table, class Io>
 void launch_columns(const Io& io, long long transforms, cudaStream_t stream)
 {
@@ -87,7 +118,8 @@ void launch_columns(const Io& io, long long transforms, cudaStream_t stream)
         return;
     }
     constexpr int C = columns_per_cta<PL>();
-    auto kernel = column_kernel<PL, C, Inv, B, Table, Io>;
+    constexpr bool Prefetch = column_prefetch<Io>::value && PL::N >= 64 && PL::N <= 512;
+    auto kernel = column_kernel<PL, C, Inv, B, Table, Io, false, Prefetch>;
     constexpr std::size_t smem = column_smem_bytes<PL, C>();
     static std::atomic<int> cache[kMaxDevices];
     const float2* tw = Table ? twiddles::pass_table(PL::N, PL::E) : nullptr;
@@ -109,8 +141,10 @@ __device__ __forceinline__ int mode_row(int pos, int n, int m1)
 }
 
 // Columns of `slabs` row-major arrays of N rows by `cols` columns, pruned as Backend::columns
-// describes.
+// describes. In place or out of place: a tile's columns are its own, so its loads may run one
+// tile ahead.
 struct StridedIo {
+    static constexpr bool kPrefetch = true;
     const float2* x;
     float2* y;
     int cols;
@@ -265,10 +299,12 @@ struct FourStepIo {
     }
 };
 
-// Strided column plans with the CTAs per SM that the register budget must allow, from a sweep
-// on B200 (256-point columns of 256 fields x 129: 32.3 us at the compiler's own budget, two CTAs
-// per SM; 29.7 us at three; 512-point columns 41.1 -> 38.8 us at two).
-__host__ __device__ constexpr int column_min_blocks(int n) { return n == 256 ? 3 : n == 512 ? 2 : 1; }
+// Strided column plans with the CTAs per SM that the register budget must allow, from sweeps
+// on B200. Without the prefetch, 256-point columns of 256 fields x 129 took 32.3 us at the
+// compiler's own budget (two CTAs per SM) and 29.7 us at three; with it (32 more registers),
+// 27.2 us at two, while three spill. 512-point columns: 38.8 us at two CTAs per SM without the
+// prefetch, 29.8 us at one with it.
+__host__ __device__ constexpr int column_min_blocks(int n) { return n == 256 ? 2 : 1; }
 
 template <int N>
 using ColumnPlan = Plan<N, default_e(N), false, default_threads(N), column_min_blocks(N)>;

@@ -42,8 +42,9 @@ using PlanFor = Plan<N, default_e(N), false, default_threads(N)>;
 // (no per-CTA set-up left once the tables are in global memory, and the hardware scheduler
 // balances the last wave: 1024-point complex transforms 47.3 -> 44.5 us), and whether the next
 // tile's input is loaded while this one computes (4096-point real forward 30.9 -> 28.8 us,
-// 256-point real 33.0 -> 31.5 us forward and 29.6 -> 29.0 us inverse; elsewhere it measured
-// slower). Each entry is the
+// 256-point real 29.6 -> 29.0 us inverse; elsewhere it measured slower; the 256-point real
+// forward, once its twiddles were derived, runs best as one CTA per tile with a budget of 5 CTAs
+// per SM: 30.7 us persistent with the prefetch, 27.3 us). Each entry is the
 // best of a sweep on B200 at 2^24 points per call. The pattern: reading the twiddles from global
 // memory halves the shared memory of the real-transform kernels and lets the compiler hoist the
 // twiddle loads past the exchanges' barriers (1024 real points: 38.9 -> 30.0 us; 4096: 39.1 ->
@@ -76,7 +77,7 @@ __host__ __device__ constexpr RowChoice row_choice(RowKind k, int n)
          : n == 16     ? RowChoice{kMinThreads, 1, !r2c, false, false}
          : n == 32     ? RowChoice{kMinThreads, 1, true, false, true}
          : n == 64     ? RowChoice{kMinThreads, 1, false, false, true}
-         : n == 128    ? RowChoice{128, 4, false, false, true, true}
+         : n == 128    ? (r2c ? RowChoice{128, 5, false, false, false, false} : RowChoice{128, 4, false, false, true, true})
          : n == 512    ? RowChoice{128, r2c ? 3 : 4, r2c, false, true}
          : n <= 1024   ? RowChoice{128, 4, false, false, true}
          : n == 2048   ? RowChoice{128, r2c ? 5 : 6, false, false, r2c, r2c}

@@ -317,6 +317,9 @@ std::size_t c2c_pruned_work(const Impl& impl, int n, int, long long batch)
     return impl.has_pruned() ? 0 : count3(batch, 1, n);
 }
 
+// Whether spectral_rfft2_modes takes the tensor-core forward (pruned_tc.cu) where it fits.
+constexpr bool kAutoTensorModes = false;
+
 bool fused_pruned(const Impl& impl, int n1, int n2, int m1, int m2)
 {
     return impl.backend->pruned2d_supported != nullptr
@@ -592,8 +595,16 @@ int spectral_irfft2_modes_workspace(const char* impl, int n1, int n2, int m1, in
 int spectral_rfft2_modes(const char* impl, const float* x, void* modes, int n1, int n2, int m1,
                          int m2, long long batch, void* work, void* stream)
 {
+    return spectral_rfft2_modes_method(impl, x, modes, n1, n2, m1, m2, batch, SPECTRAL_MODES_AUTO, work, stream);
+}
+
+int spectral_rfft2_modes_method(const char* impl, const float* x, void* modes, int n1, int n2, int m1,
+                                int m2, long long batch, int method, void* work, void* stream)
+{
     return guarded([&] {
         const Impl& i = find(impl);
+        need(method >= SPECTRAL_MODES_AUTO && method <= SPECTRAL_MODES_TENSOR,
+             "rfft2_modes: method must be SPECTRAL_MODES_AUTO, _FP32 or _TENSOR");
         need_aligned(x, "rfft2_modes");
         need_aligned(modes, "rfft2_modes");
         check_pruned_2d(i, n1, n2, m1, m2, batch);
@@ -601,7 +612,16 @@ int spectral_rfft2_modes(const char* impl, const float* x, void* modes, int n1, 
         auto* ms = static_cast<float2*>(modes);
         auto* ws = static_cast<float2*>(work);
         const cudaStream_t s = as_stream(stream);
-        if (fused_pruned(i, n1, n2, m1, m2)) {
+        const bool fused = fused_pruned(i, n1, n2, m1, m2);
+        const bool tensor_fits = fused && pruned_tc_forward_fits(x, n1, n2, m1, m2, batch);
+        need(method != SPECTRAL_MODES_TENSOR || tensor_fits,
+             "rfft2_modes: the tensor-core method needs an engine implementation, n1 = n2 = 128, "
+             "m2 <= 16 and a 16-byte aligned x");
+        if (method == SPECTRAL_MODES_TENSOR || (method == SPECTRAL_MODES_AUTO && tensor_fits && kAutoTensorModes)) {
+            pruned_tc_forward(x, ms, m1, m2, batch, s);
+            return;
+        }
+        if (fused) {
             i.backend->rfft2_modes(x, ms, n1, n2, m1, m2, batch, s);
             return;
         }

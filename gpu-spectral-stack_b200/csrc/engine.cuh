@@ -201,11 +201,18 @@ __device__ __forceinline__ void fill_pass_twiddles(float2* tw, const float2* __r
     }
 }
 
-template <int P, bool CtaSync>
+// The barrier around an exchange. CtaSync 0: the transform's own threads (group_sync); 1: the
+// whole CTA; otherwise the named barrier CtaSync >> 10 (1 .. 15) over CtaSync & 1023 threads, for
+// warp-specialized kernels in which only one group of warps runs the passes.
+template <int P, int CtaSync>
 __device__ __forceinline__ void exchange_sync()
 {
-    if constexpr (CtaSync) {
+    if constexpr (CtaSync == 1) {
         __syncthreads();
+    } else if constexpr (CtaSync > 1) {
+        static_assert((CtaSync >> 10) >= 1 && (CtaSync >> 10) <= 15 && (CtaSync & 1023) % 32 == 0,
+                      "named barrier: id 1 .. 15, whole warps");
+        asm volatile("bar.sync %0, %1;" ::"n"(CtaSync >> 10), "n"(CtaSync & 1023) : "memory");
     } else {
         group_sync<P>();
     }
@@ -234,7 +241,7 @@ __device__ __forceinline__ int butterfly(int t, int b)
 // caller offsets `buf` by c). Either way a thread's write indices are one runtime base per
 // butterfly plus compile-time offsets, and for the plain layout L divides P, so k = t mod L
 // and one set of twiddles serves all Q butterflies.
-template <class PL, int S, bool Inv, int B, int Stride, bool CtaSync, bool Mirror, bool MirrorNext,
+template <class PL, int S, bool Inv, int B, int Stride, int CtaSync, bool Mirror, bool MirrorNext,
           int Derive = 0>
 __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
 {
@@ -398,7 +405,7 @@ __device__ __forceinline__ void pass(float2 (&v)[PL::E], int t, float2* buf, con
 // above) instead of the table; 2 and 3, radix-16 passes also form 9 of their 15 twiddles from
 // the other 6 (see pass). For the computed-twiddle variants, whose tables are not correctly
 // rounded either.
-template <class PL, bool Inv, int B, int Stride = 0, bool CtaSync = false, bool MirrorFirst = false,
+template <class PL, bool Inv, int B, int Stride = 0, int CtaSync = 0, bool MirrorFirst = false,
           bool MirrorLast = false, int Derive = 0>
 __device__ __forceinline__ void run_passes(float2 (&v)[PL::E], int t, float2* buf, const float2* tw)
 {

@@ -5,6 +5,7 @@
 #include "dft.cuh"
 #include "engine.cuh"
 
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -151,6 +152,49 @@ const float2* half_turn(int n)
     return get(Key{1, n, 0}, n + 1, [&](std::vector<float2>& t) {
         for (int k = 0; k <= n; ++k) {
             t[static_cast<std::size_t>(k)] = forward_factor(k, 2LL * n);
+        }
+    });
+}
+
+namespace {
+
+// a rounded to TF32 (10 fraction bits), to nearest with ties away from zero, as the tensor-core
+// kernels split their FP32 operands on the GPU.
+float tf32_round_host(float a)
+{
+    unsigned u = 0;
+    std::memcpy(&u, &a, sizeof u);
+    u = (u + 0x1000u) & 0xFFFFE000u;
+    float r = 0.0f;
+    std::memcpy(&r, &u, sizeof r);
+    return r;
+}
+
+}  // namespace
+
+const float2* tf32_dft_rows(int n, int m)
+{
+    if (n % 8 != 0 || m < 1 || m > kTf32DftOutputs) {
+        throw InvalidArgument("tf32_dft_rows: n must be a multiple of 8 and 1 <= m <= 16");
+    }
+    const long long floats = 4LL * kTf32DftOutputs * n;
+    return get(Key{7, n, m}, floats / 2, [&](std::vector<float2>& t) {
+        float* f = reinterpret_cast<float*>(t.data());
+        constexpr int kRows = 4 * kTf32DftOutputs;
+        constexpr int kLboFloats = kRows / 8 * 32;  // one 8-row x 16-byte core matrix per 32 floats
+        for (int b = 0; b < kRows; ++b) {
+            const int k = b % kTf32DftOutputs;     // output index of this row
+            const int part = b / kTf32DftOutputs;  // 0 cos hi, 1 -sin hi, 2 cos lo, 3 -sin lo
+            for (int j = 0; j < n; ++j) {
+                float v = 0.0f;
+                if (k < m) {
+                    const dft::CosSin w = dft::cs2pi(static_cast<long long>(k) * j, n);
+                    const double exact = (part % 2 == 0) ? w.c : -w.s;
+                    const float hi = tf32_round_host(static_cast<float>(exact));
+                    v = part < 2 ? hi : tf32_round_host(static_cast<float>(exact - static_cast<double>(hi)));
+                }
+                f[(j / 4) * kLboFloats + (b / 8) * 32 + (b % 8) * 4 + j % 4] = v;
+            }
         }
     });
 }

@@ -31,4 +31,15 @@ const float2* half_turn_computed(int n);
 // products of two such tables).
 const float2* turn(long long total, int count);
 
+// The row-DFT operand of the tensor-core pruned forward (pruned_tc.cu): the first m (<= 16)
+// outputs of n-point real rows as 64 rows of n TF32 values, cos(2 pi k j / n) and
+// -sin(2 pi k j / n) for k = 0 .. 15 (zero for k >= m), each split into a hi part (the value
+// rounded to TF32) and a lo part (the rest, rounded to TF32): rows 0-15 cos hi, 16-31 -sin hi,
+// 32-47 cos lo, 48-63 -sin lo. Stored in the tensor core's canonical K-major layout without
+// swizzle: value (row b, j) at float (j / 4) 256 + (b / 8) 32 + (b % 8) 4 + j % 4, i.e. core
+// matrices of 8 rows x 16 bytes, 128 bytes apart along the rows and 1 KiB apart along j.
+// 64 n floats, returned as float2 storage.
+constexpr int kTf32DftOutputs = 16;
+const float2* tf32_dft_rows(int n, int m);
+
 }  // namespace spectral::twiddles

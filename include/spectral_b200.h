@@ -163,6 +163,21 @@ SPECTRAL_API int spectral_irfft2_modes_workspace(const char* impl, int n1, int n
  * n1-m1 .. n1-1; columns 0 .. m2-1 (spectral.reference.rfft2_truncate). */
 SPECTRAL_API int spectral_rfft2_modes(const char* impl, const float* x, void* modes, int n1, int n2, int m1,
                          int m2, long long batch, void* work, void* stream);
+/* spectral_rfft2_modes with the row stage's method chosen by the caller (no reference
+ * counterpart):
+ *   SPECTRAL_MODES_AUTO    what spectral_rfft2_modes uses;
+ *   SPECTRAL_MODES_FP32    the FP32 FFT engine for rows and columns (one fused kernel);
+ *   SPECTRAL_MODES_TENSOR  the rows as a GEMM with the kept DFT outputs on the tcgen05 tensor
+ *                          cores, every FP32 operand split into two TF32 parts (three products
+ *                          per multiply: FP32-level error); the columns by the FFT engine. Needs
+ *                          an engine implementation, n1 = n2 = 128, m2 <= 16 and a 16-byte
+ *                          aligned x; other shapes are refused. */
+#define SPECTRAL_MODES_AUTO 0
+#define SPECTRAL_MODES_FP32 1
+#define SPECTRAL_MODES_TENSOR 2
+SPECTRAL_API int spectral_rfft2_modes_method(const char* impl, const float* x, void* modes, int n1, int n2,
+                                             int m1, int m2, long long batch, int method, void* work,
+                                             void* stream);
 /* The inverse: every other mode zero, then irfft2 (spectral.reference.irfft2_from_modes). */
 SPECTRAL_API int spectral_irfft2_modes(const char* impl, const void* modes, float* y, int n1, int n2, int m1,
                           int m2, long long batch, void* work, void* stream);

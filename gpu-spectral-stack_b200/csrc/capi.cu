@@ -318,7 +318,7 @@ std::size_t c2c_pruned_work(const Impl& impl, int n, int, long long batch)
 }
 
 // Whether spectral_rfft2_modes takes the tensor-core forward (pruned_tc.cu) where it fits.
-constexpr bool kAutoTensorModes = false;
+constexpr bool kAutoTensorModes = true;
 
 bool fused_pruned(const Impl& impl, int n1, int n2, int m1, int m2)
 {

@@ -24,13 +24,15 @@
 //
 // Data flow, per CTA (one per SM, persistent over fields), warp-specialized:
 //   - warp 0: TMA loads of the field's rows in chunks of 32 values (boxes of 128 rows x 128 bytes,
-//     128-byte swizzle), kStages chunks in flight;
-//   - warps 2-5: each thread owns one row (TMEM lane): it reads its 32 values of a chunk from
-//     shared memory, splits them, and stores the hi and lo parts into the chunk's A operand in
-//     tensor memory (tcgen05.st; TMEM lanes are rows, columns are K), 4 chunk stages;
+//     128-byte swizzle), 10 chunks (160 KiB) in flight: a load takes about 2.5 us from issue to
+//     arrival at this kernel's bandwidth, and the stages in flight set the bandwidth;
+//   - warps 2-9, two sets of 4 taking alternate chunks: each thread owns one row (TMEM lane): it
+//     reads its 32 values of a chunk from shared memory (then releases the stage), splits them,
+//     and stores the hi and lo parts into the chunk's A operand in tensor memory (tcgen05.st;
+//     TMEM lanes are rows, columns are K), 4 chunk stages;
 //   - warp 1: one elected lane issues the MMAs (A from tensor memory, F from shared memory) into
 //     one of two field accumulators and commits them;
-//   - warps 6-9 and 10-13: two column groups taking alternate fields. A group reads its field's
+//   - warps 10-13 and 14-17: two column groups taking alternate fields. A group reads its field's
 //     accumulators (one row per thread), adds the three products, writes the 128 x 16 complex
 //     tile to shared memory, runs the column passes (named barriers over its 128 threads) and
 //     stores the kept modes.
@@ -67,7 +69,7 @@ constexpr int kFRows = 4 * kMaxM2;                 // cos hi, -sin hi, cos lo, -
 constexpr int kLbo = kFRows / 8 * 128;             // F: bytes between core matrices along K
 constexpr int kSbo = 128;                          // F: bytes between 8-row groups
 constexpr int kFBytes = kN2 / 4 * kLbo;            // 32 KiB
-constexpr int kStages = 6;                         // x chunks in shared memory
+constexpr int kStages = 10;                        // x chunks in shared memory (160 KiB in flight)
 constexpr int kAStages = 4;                        // split chunks in tensor memory
 constexpr int kBoxBytes = kN1 * kKc * 4;           // 16 KiB
 constexpr uint32_t kTmemCols = 512;
@@ -82,10 +84,11 @@ static_assert(kCW == kMaxM2, "one column group covers every kept column");
 constexpr int kColEntries = kN1 * kCW;             // a group's [row][column] tile (float2)
 constexpr int kTwEntries = (CP::TW + 1) & ~1;
 
-constexpr int kSplitWarp0 = 2;                     // warps 2-5 split, one per TMEM lane quarter
-constexpr int kColWarp0 = kSplitWarp0 + 4;
+constexpr int kSplitWarp0 = 2;                     // two sets of 4 split warps (one per TMEM lane
+constexpr int kSplitSets = 2;                      // quarter) taking alternate chunks: warps 2-9
+constexpr int kColWarp0 = kSplitWarp0 + 4 * kSplitSets;
 constexpr int kGroups = 2;
-constexpr int kThreads = (kColWarp0 + 4 * kGroups) * 32;  // 448
+constexpr int kThreads = (kColWarp0 + 4 * kGroups) * 32;  // 576
 
 constexpr int kOffX = 0;
 constexpr int kOffF = kOffX + kStages * kBoxBytes;
@@ -399,10 +402,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp < kColWarp0) {
-        // Split warps: thread = row r of the field = TMEM lane r.
+        // Split warps: thread = row r of the field = TMEM lane r; set `set` takes the chunks
+        // q = set, set + kSplitSets, ..
         const int r = (warp & 3) * 32 + lane;
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-        for (long long q = 0; q < chunks; ++q) {
+        const int set = (warp - kSplitWarp0) / 4;
+        for (long long q = set; q < chunks; q += kSplitSets) {
             const int s = static_cast<int>(q % kStages);
             const int a = static_cast<int>(q % kAStages);
             bool ok = tma::mbar_wait(&sfull[s], static_cast<unsigned>(q / kStages) & 1u);
@@ -429,6 +434,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     lo[4 * j + t] = __float_as_uint(tf32_round(e[t] - h));
                 }
             }
+            // The chunk's values are in registers: its stage may take the next load already.
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&sempty[s]);
+            }
             const uint32_t acol = tmem + lane_base + kACol0 + static_cast<uint32_t>(a) * kACols;
             tmem_store32(acol, hi);
             tmem_store32(acol + kKc, lo);
@@ -437,7 +447,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&afull[a]);
-                mbar_arrive(&sempty[s]);
             }
         }
     } else if (warp < kColWarp0 + 4) {

@@ -57,10 +57,13 @@ void set_last_error(const std::string& message);
 int run_fft2_c2r_strided(const char* impl, const void* x, float* y, int n1, int n2,
                          long long batch, float2* work, std::size_t work_values, void* stream);
 
-// The pruned 2D real forward of 128 x 128 fields with its row stage on the tensor cores
-// (pruned_tc.cu): fits when n1 = n2 = 128, m2 <= 16, x is 16-byte aligned and fields * 128 rows
-// address with 32-bit coordinates. Same mode layout as Backend::rfft2_modes.
-bool pruned_tc_forward_fits(const void* x, int n1, int n2, int m1, int m2, long long fields);
+// The pruned 2D real transforms of 128 x 128 fields with their row stage on the tensor cores
+// (pruned_tc.cu): fit when n1 = n2 = 128, m2 <= 16, the real array (x forward, y inverse) is
+// 16-byte aligned and fields * 128 rows address with 32-bit coordinates. Same mode layout as
+// Backend::rfft2_modes / irfft2_modes.
+bool pruned_tc_fits(const void* real, int n1, int n2, int m1, int m2, long long fields);
 void pruned_tc_forward(const float* x, float2* modes, int m1, int m2, long long fields, cudaStream_t stream);
+// The inverse: the columns by the FFT engine, the real rows as a GEMM on the tensor cores.
+void pruned_tc_inverse(const float2* modes, float* y, int m1, int m2, long long fields, cudaStream_t stream);
 
 }  // namespace spectral

@@ -317,8 +317,10 @@ std::size_t c2c_pruned_work(const Impl& impl, int n, int, long long batch)
     return impl.has_pruned() ? 0 : count3(batch, 1, n);
 }
 
-// Whether spectral_rfft2_modes takes the tensor-core forward (pruned_tc.cu) where it fits.
+// Whether spectral_rfft2_modes / spectral_irfft2_modes take the tensor-core kernels
+// (pruned_tc.cu) where they fit.
 constexpr bool kAutoTensorModes = true;
+constexpr bool kAutoTensorInverse = false;
 
 bool fused_pruned(const Impl& impl, int n1, int n2, int m1, int m2)
 {
@@ -613,7 +615,7 @@ int spectral_rfft2_modes_method(const char* impl, const float* x, void* modes, i
         auto* ws = static_cast<float2*>(work);
         const cudaStream_t s = as_stream(stream);
         const bool fused = fused_pruned(i, n1, n2, m1, m2);
-        const bool tensor_fits = fused && pruned_tc_forward_fits(x, n1, n2, m1, m2, batch);
+        const bool tensor_fits = fused && pruned_tc_fits(x, n1, n2, m1, m2, batch);
         need(method != SPECTRAL_MODES_TENSOR || tensor_fits,
              "rfft2_modes: the tensor-core method needs an engine implementation, n1 = n2 = 128, "
              "m2 <= 16 and a 16-byte aligned x");
@@ -640,8 +642,16 @@ int spectral_rfft2_modes_method(const char* impl, const float* x, void* modes, i
 int spectral_irfft2_modes(const char* impl, const void* modes, float* y, int n1, int n2, int m1,
                           int m2, long long batch, void* work, void* stream)
 {
+    return spectral_irfft2_modes_method(impl, modes, y, n1, n2, m1, m2, batch, SPECTRAL_MODES_AUTO, work, stream);
+}
+
+int spectral_irfft2_modes_method(const char* impl, const void* modes, float* y, int n1, int n2, int m1,
+                                 int m2, long long batch, int method, void* work, void* stream)
+{
     return guarded([&] {
         const Impl& i = find(impl);
+        need(method >= SPECTRAL_MODES_AUTO && method <= SPECTRAL_MODES_TENSOR,
+             "irfft2_modes: method must be SPECTRAL_MODES_AUTO, _FP32 or _TENSOR");
         need_aligned(modes, "irfft2_modes");
         need_aligned(y, "irfft2_modes");
         check_pruned_2d(i, n1, n2, m1, m2, batch);
@@ -649,7 +659,16 @@ int spectral_irfft2_modes(const char* impl, const void* modes, float* y, int n1,
         const auto* ms = static_cast<const float2*>(modes);
         auto* ws = static_cast<float2*>(work);
         const cudaStream_t s = as_stream(stream);
-        if (fused_pruned(i, n1, n2, m1, m2)) {
+        const bool fused = fused_pruned(i, n1, n2, m1, m2);
+        const bool tensor_fits = fused && pruned_tc_fits(y, n1, n2, m1, m2, batch);
+        need(method != SPECTRAL_MODES_TENSOR || tensor_fits,
+             "irfft2_modes: the tensor-core method needs an engine implementation, n1 = n2 = 128, "
+             "m2 <= 16 and a 16-byte aligned y");
+        if (method == SPECTRAL_MODES_TENSOR || (method == SPECTRAL_MODES_AUTO && tensor_fits && kAutoTensorInverse)) {
+            pruned_tc_inverse(ms, y, m1, m2, batch, s);
+            return;
+        }
+        if (fused) {
             i.backend->irfft2_modes(ms, y, n1, n2, m1, m2, batch, s);
             return;
         }

@@ -116,6 +116,13 @@ __device__ __forceinline__ uint64_t f_desc(uint32_t addr)
            | (static_cast<uint64_t>((kSbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
 }
 
+template <int Lbo>
+__device__ __forceinline__ uint64_t f_desc_lbo(uint32_t addr)
+{
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((Lbo >> 4) & 0x3FFF) << 16)
+           | (static_cast<uint64_t>((kSbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+
 __device__ __forceinline__ float tf32_round(float a)
 {
     return __uint_as_float((__float_as_uint(a) + 0x1000u) & 0xFFFFE000u);
@@ -481,6 +488,309 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// --- the inverse (irfft2_from_modes) ------------------------------------------------------------
+//
+// Columns first: the m2 kept columns' 128-point inverse transforms (the radix-8 engine, from the
+// 2 m1 kept rows), which leave R[n1, k] for every row n1 and k < m2. Then each row's real inverse
+//   y[n1, n2] = sum_k c_k (Re R[n1, k] cos(2 pi k n2 / 128) - Im R[n1, k] sin(2 pi k n2 / 128)) / 128^2,
+// c_0 = 1 and c_k = 2 otherwise (the Hermitian partner of each kept column; Im R[n1, 0] meets
+// sin 0 = 0 and drops out as a real inverse drops it), is Y = A' C'^T: A' (M = 128 rows, K = 32)
+// holds c_k Re R / 128^2 and -c_k Im R / 128^2 (exact scalings by powers of two), C' (N = 128
+// output positions, K = 32) holds cos and sin (twiddles::tf32_idft_rows). Both are split into
+// TF32 hi and lo parts; the three products x_hi C_hi, x_hi C_lo and x_lo C_hi accumulate in one
+// accumulator (32 terms per output: its per-MMA rounding stays at the FP32 level).
+//
+// Warps: 0 issues the MMAs (3 per 8 values of K, N = 128); 1-4 (the epilogue) read a field's
+// accumulator (one output row per thread, 32 columns at a time), stage the rows in shared memory
+// in the 128-byte swizzled box layout and store each 128 x 32 box with one TMA store; 5-8 and
+// 9-12, two column groups on alternate fields, load the kept modes (the next field's a field
+// ahead), run the column passes, turn the column-major result into rows through a shared-memory
+// tile and store each row's split A' into tensor memory. Accumulators: 2 x 128 columns; A': 4
+// fields x 64 columns.
+
+constexpr int kIK = 2 * kMaxM2;                    // 32: cos and sin coefficients of a row
+constexpr int kIFRows = 2 * kN2;                   // C' hi rows, then lo rows
+constexpr int kILbo = kIFRows / 8 * 128;           // 4 KiB
+constexpr int kIFBytes = kIK / 4 * kILbo;          // 32 KiB
+constexpr int kIDStages = 2;
+constexpr int kIAStages = 4;
+constexpr uint32_t kIDCols = 128;
+constexpr uint32_t kIACol0 = kIDStages * kIDCols;
+constexpr uint32_t kIACols = 2 * kIK;              // hi 32 + lo 32
+static_assert(kIACol0 + kIAStages * kIACols <= kTmemCols, "tensor memory");
+constexpr int kIOutBufs = kN2 / kKc;               // one staging box per 32 output columns
+constexpr int kIEpiWarp0 = 1;
+constexpr int kIColWarp0 = kIEpiWarp0 + 4;
+constexpr int kIThreads = (kIColWarp0 + 4 * kGroups) * 32;  // 416
+constexpr int kIEpiSync = (3 << 10) | 128;         // named barrier 3 over the epilogue warps
+constexpr int kIOffOut = 0;
+constexpr int kIOffF = kIOffOut + kIOutBufs * kBoxBytes;
+constexpr int kIOffCol = kIOffF + kIFBytes;
+constexpr int kIOffTw = kIOffCol + kGroups * kColEntries * 8;
+constexpr int kIOffBar = kIOffTw + kTwEntries * 8;
+constexpr int kIBars = 2 * kIAStages + 2 * kIDStages;
+constexpr int kISmemBytes = kIOffBar + kIBars * 8 + 16 + 1024;
+static_assert(kISmemBytes <= 227 * 1024, "shared memory");
+static_assert(kISmemBytes > 114 * 1024, "one CTA per SM: the CTA takes all of tensor memory");
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+                 "r"(tma::smem_addr(src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N committed bulk stores of this thread still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+template <int G>
+__device__ __forceinline__ bool inverse_column_group(const float2* __restrict__ modes, uint64_t* afull,
+                                                     uint64_t* aempty, uint32_t tmem, float2* tile,
+                                                     const float2* twc, long long nf, int m1, int m2)
+{
+    constexpr int kSync = ((1 + G) << 10) | 128;
+    const int tid = static_cast<int>(threadIdx.x);
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int gt = tid - (kIColWarp0 + 4 * G) * 32;
+    const int r = (warp & 3) * 32 + lane;
+    const int cc = gt % kCW;
+    const int ct = gt / kCW;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const float2 zero = make_float2(0.0f, 0.0f);
+    float2 next[CP::E];
+    auto load = [&](long long i) {
+        const long long f = static_cast<long long>(blockIdx.x) + i * gridDim.x;
+        const float2* mf = modes + f * (2LL * m1 * m2);
+#pragma unroll
+        for (int e = 0; e < CP::E; ++e) {
+            const int row = engine::mode_row(ct + e * CP::P, kN1, m1);
+            next[e] = (i < nf && cc < m2 && row >= 0) ? __ldg(mf + row * m2 + cc) : zero;
+        }
+    };
+    load(G);
+    constexpr float kScale = 1.0f / (kN1 * kN2);  // a power of two: the scalings below are exact
+    for (long long i = G; i < nf; i += kGroups) {
+        float2 v[CP::E];
+#pragma unroll
+        for (int e = 0; e < CP::E; ++e) {
+            v[e] = next[e];
+        }
+        load(i + kGroups);
+        engine::run_passes<CP, true, 8, kCW, kSync>(v, ct, tile + cc, twc);
+        // The last exchange's reads are done (its trailing barrier): the tile takes the result.
+#pragma unroll
+        for (int e = 0; e < CP::E; ++e) {
+            const int row = ct + e * CP::P;
+            tile[row * kCW + (cc ^ (row & 15))] = v[e];
+        }
+        engine::exchange_sync<1, kSync>();
+        uint32_t hi[kIK], lo[kIK];
+#pragma unroll
+        for (int k = 0; k < kCW; ++k) {
+            const float2 z = tile[r * kCW + (k ^ (r & 15))];
+            const float c = k == 0 ? kScale : 2.0f * kScale;
+            const float re = z.x * c;
+            const float im = -z.y * c;
+            const float hre = tf32_round(re);
+            const float him = tf32_round(im);
+            hi[k] = __float_as_uint(hre);
+            lo[k] = __float_as_uint(tf32_round(re - hre));
+            hi[kCW + k] = __float_as_uint(him);
+            lo[kCW + k] = __float_as_uint(tf32_round(im - him));
+        }
+        engine::exchange_sync<1, kSync>();  // the tile's reads done before the next field's passes
+        const int a = static_cast<int>(i % kIAStages);
+        const bool ok = i < kIAStages || tma::mbar_wait(&aempty[a], static_cast<unsigned>(i / kIAStages - 1) & 1u);
+        if (!group_all<(kSync >> 10)>(ok)) {
+            return false;
+        }
+        fence_after_sync();
+        const uint32_t acol = tmem + lane_base + kIACol0 + static_cast<uint32_t>(a) * kIACols;
+        tmem_store32(acol, hi);
+        tmem_store32(acol + kIK, lo);
+        tmem_wait_store();
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&afull[a]);
+        }
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(kIThreads, 1)
+    pruned_tc_inverse_kernel(const __grid_constant__ CUtensorMap map_y, const float2* __restrict__ modes,
+                             long long fields, int m1, int m2, const float2* __restrict__ f_rows,
+                             const float2* __restrict__ twc_g, unsigned* fault)
+{
+    wait_for_previous_grid();
+    allow_next_grid();
+    extern __shared__ unsigned char smem_base[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_base) + 1023) & ~static_cast<uintptr_t>(1023));
+    unsigned char* outs = smem + kIOffOut;
+    unsigned char* fs = smem + kIOffF;
+    auto* colbuf = reinterpret_cast<float2*>(smem + kIOffCol);
+    auto* twc = reinterpret_cast<float2*>(smem + kIOffTw);
+    auto* afull = reinterpret_cast<uint64_t*>(smem + kIOffBar);  // a field's A' stored (4 warps)
+    uint64_t* aempty = afull + kIAStages;                          // its MMAs completed
+    uint64_t* dfull = aempty + kIAStages;                          // a field's MMAs completed
+    uint64_t* dempty = dfull + kIDStages;                          // its accumulator read (4 warps)
+    auto* tmem_slot = reinterpret_cast<uint32_t*>(dempty + kIDStages);
+
+    const int tid = static_cast<int>(threadIdx.x);
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+
+    for (int i = tid; i < kIFBytes / 8; i += kIThreads) {
+        reinterpret_cast<float2*>(fs)[i] = f_rows[i];
+    }
+    engine::fill_pass_twiddles<CP, true>(twc, twc_g);
+    tma::fence_proxy_async();
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         tma::smem_addr(tmem_slot)),
+                     "n"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int a = 0; a < kIAStages; ++a) {
+            tma::mbar_init(&afull[a], 4);
+            tma::mbar_init(&aempty[a], 1);
+        }
+        for (int d = 0; d < kIDStages; ++d) {
+            tma::mbar_init(&dfull[d], 1);
+            tma::mbar_init(&dempty[d], 4);
+        }
+        tma::fence_mbar_init();
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    const long long bx = blockIdx.x;
+    const long long nf = fields > bx ? (fields - 1 - bx) / gridDim.x + 1 : 0;
+    bool failed = false;
+    long long committed = 0;  // warp 0: fields whose MMAs were committed
+
+    if (warp == 0) {
+        const uint32_t f0 = tma::smem_addr(fs);
+        for (long long i = 0; i < nf; ++i) {
+            const uint32_t d = static_cast<uint32_t>(i % kIDStages);
+            const int a = static_cast<int>(i % kIAStages);
+            bool ok = i < kIDStages || tma::mbar_wait(&dempty[d], static_cast<unsigned>(i / kIDStages - 1) & 1u);
+            ok = ok && tma::mbar_wait(&afull[a], static_cast<unsigned>(i / kIAStages) & 1u);
+            if (!__all_sync(0xffffffffu, ok)) {
+                failed = true;
+                break;
+            }
+            fence_after_sync();
+            if (elect_one()) {
+                const uint32_t dcol = tmem + d * kIDCols;
+                const uint32_t acol = tmem + kIACol0 + static_cast<uint32_t>(a) * kIACols;
+#pragma unroll
+                for (int j = 0; j < kIK / 8; ++j) {
+                    const uint32_t kstep = f0 + static_cast<uint32_t>(j * 2 * kILbo);
+                    const uint64_t c_hi = f_desc_lbo<kILbo>(kstep);
+                    const uint64_t c_lo = f_desc_lbo<kILbo>(kstep + kN2 / 8 * 128);
+                    mma_ts(dcol, acol + 8 * j, c_hi, idesc(kN2), j > 0 ? 1u : 0u);  // x_hi C_hi
+                    mma_ts(dcol, acol + 8 * j, c_lo, idesc(kN2), 1u);               // x_hi C_lo
+                    mma_ts(dcol, acol + kIK + 8 * j, c_hi, idesc(kN2), 1u);         // x_lo C_hi
+                }
+                mma_commit(&aempty[a]);
+                mma_commit(&dfull[d]);
+            }
+            __syncwarp();
+            ++committed;
+        }
+    } else if (warp < kIColWarp0) {
+        // Epilogue: thread = output row r of the field = TMEM lane r.
+        const int et = tid - kIEpiWarp0 * 32;
+        const int r = (warp & 3) * 32 + lane;
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        for (long long i = 0; i < nf; ++i) {
+            const int d = static_cast<int>(i % kIDStages);
+            const bool ok = tma::mbar_wait(&dfull[d], static_cast<unsigned>(i / kIDStages) & 1u);
+            if (!group_all<(kIEpiSync >> 10)>(ok)) {
+                failed = true;
+                break;
+            }
+            fence_after_sync();
+            const long long f = bx + i * gridDim.x;
+#pragma unroll 1
+            for (int c = 0; c < kIOutBufs; ++c) {
+                if (et == 0) {
+                    bulk_wait_read<kIOutBufs - 1>();  // box c of the previous field has left
+                }
+                engine::exchange_sync<1, kIEpiSync>();
+                uint32_t v[32];
+                tmem_load32(tmem + lane_base + static_cast<uint32_t>(d) * kIDCols + 32 * c, v);
+                tmem_wait_load();
+                if (c == kIOutBufs - 1) {
+                    fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&dempty[d]);
+                    }
+                }
+                // Row r of the box at r * 128 bytes, 16-byte piece j at piece j ^ (r mod 8): the
+                // TMA's 128-byte swizzle, and 8 distinct bank groups per quarter-warp.
+                unsigned char* row = outs + c * kBoxBytes + r * 128;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) =
+                        make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
+                tma::fence_proxy_async();
+                engine::exchange_sync<1, kIEpiSync>();
+                if (et == 0) {
+                    tma_store_2d(&map_y, outs + c * kBoxBytes, c * kKc, static_cast<int>(f * kN1));
+                    bulk_commit();
+                }
+            }
+        }
+        if (et == 0) {
+            bulk_wait_all();
+        }
+    } else if (warp < kIColWarp0 + 4) {
+        failed = !inverse_column_group<0>(modes, afull, aempty, tmem, colbuf, twc, nf, m1, m2);
+    } else {
+        failed = !inverse_column_group<1>(modes, afull, aempty, tmem, colbuf + kColEntries, twc, nf, m1, m2);
+    }
+
+    if (__syncthreads_or(failed)) {
+        bool drained = true;
+        if (tid == 0) {
+            atomicOr(fault, tma::kFaultWaitTimeout);
+            if (committed > 0) {
+                const long long i = committed - 1;
+                drained = tma::mbar_wait(&aempty[i % kIAStages], static_cast<unsigned>(i / kIAStages) & 1u);
+            }
+        }
+        if (!drained) {
+            atomicOr(fault, tma::kFaultDrainTimeout);
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kTmemCols) : "memory");
+    }
+}
+
 PFN_cuTensorMapEncodeTiled encode_fn()
 {
     static std::once_flag once;
@@ -501,10 +811,50 @@ PFN_cuTensorMapEncodeTiled encode_fn()
 
 }  // namespace
 
-bool pruned_tc_forward_fits(const void* x, int n1, int n2, int m1, int m2, long long fields)
+bool pruned_tc_fits(const void* x, int n1, int n2, int m1, int m2, long long fields)
 {
     return n1 == kN1 && n2 == kN2 && m1 >= 1 && 2 * m1 <= kN1 && m2 >= 1 && m2 <= kMaxM2 && fields >= 1
            && fields <= INT_MAX / kN1 && (reinterpret_cast<unsigned long long>(x) & 15u) == 0;
+}
+
+namespace {
+
+// A 2D tensor map over fields * 128 rows of 128 floats, boxes of 32 floats x 128 rows with the
+// 128-byte swizzle.
+CUtensorMap field_rows_map(const float* base, long long fields)
+{
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kN2), static_cast<cuuint64_t>(fields) * kN1};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kN2) * sizeof(float)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kKc), static_cast<cuuint32_t>(kN1)};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult res = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                                     strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (res != CUDA_SUCCESS) {
+        throw CudaError("rfft2 modes: cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(res)) + ")");
+    }
+    return map;
+}
+
+}  // namespace
+
+void pruned_tc_inverse(const float2* modes, float* y, int m1, int m2, long long fields, cudaStream_t stream)
+{
+    static std::atomic<bool> opted[kMaxDevices];
+    const int device = current_device();
+    if (!opted[device].load(std::memory_order_relaxed)) {
+        SPECTRAL_CUDA(cudaFuncSetAttribute(pruned_tc_inverse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kISmemBytes));
+        opted[device].store(true, std::memory_order_relaxed);
+    }
+    const float2* f_rows = twiddles::tf32_idft_rows(kN2);
+    const float2* twc = twiddles::pass_table(kN1, CP::E);
+    const CUtensorMap map = field_rows_map(y, fields);
+    const long long sms = device_sm_count(device);
+    const unsigned grid = static_cast<unsigned>(fields < sms ? fields : sms);
+    launch_pdl(pruned_tc_inverse_kernel, dim3(grid), dim3(kIThreads), static_cast<std::size_t>(kISmemBytes), stream,
+               map, modes, fields, m1, m2, f_rows, twc, device_fault_word());
 }
 
 void pruned_tc_forward(const float* x, float2* modes, int m1, int m2, long long fields, cudaStream_t stream)
@@ -518,18 +868,7 @@ void pruned_tc_forward(const float* x, float2* modes, int m1, int m2, long long 
     }
     const float2* f_rows = twiddles::tf32_dft_rows(kN2, m2);
     const float2* twc = twiddles::pass_table(kN1, CP::E);
-    // x as [fields * 128 rows][128 values]; box of 32 values (128 bytes) x 128 rows.
-    CUtensorMap map;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kN2), static_cast<cuuint64_t>(fields) * kN1};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kN2) * sizeof(float)};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kKc), static_cast<cuuint32_t>(kN1)};
-    const cuuint32_t elem[2] = {1, 1};
-    const CUresult res = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(x), dims, strides,
-                                     box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (res != CUDA_SUCCESS) {
-        throw CudaError("rfft2_modes: cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(res)) + ")");
-    }
+    const CUtensorMap map = field_rows_map(x, fields);
     const long long sms = device_sm_count(device);
     const unsigned grid = static_cast<unsigned>(fields < sms ? fields : sms);
     launch_pdl(pruned_tc_forward_kernel, dim3(grid), dim3(kThreads), static_cast<std::size_t>(kSmemBytes), stream,

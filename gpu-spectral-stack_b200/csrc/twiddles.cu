@@ -199,6 +199,31 @@ const float2* tf32_dft_rows(int n, int m)
     });
 }
 
+const float2* tf32_idft_rows(int n)
+{
+    if (n % 8 != 0 || n > 256) {
+        throw InvalidArgument("tf32_idft_rows: n must be a multiple of 8 up to 256");
+    }
+    constexpr int kK = 2 * kTf32DftOutputs;  // cos k, then sin k, k = 0 .. 15
+    const long long floats = 2LL * n * kK;
+    return get(Key{8, n, 0}, floats / 2, [&](std::vector<float2>& t) {
+        float* f = reinterpret_cast<float*>(t.data());
+        const int rows = 2 * n;                // hi rows, then lo rows
+        const int lbo_floats = rows / 8 * 32;  // one 8-row x 16-byte core matrix per 32 floats
+        for (int b = 0; b < rows; ++b) {
+            const int j = b % n;  // output position n2 of this row
+            for (int kk = 0; kk < kK; ++kk) {
+                const int k = kk % kTf32DftOutputs;
+                const dft::CosSin w = dft::cs2pi(static_cast<long long>(k) * j, n);
+                const double exact = kk < kTf32DftOutputs ? w.c : w.s;
+                const float hi = tf32_round_host(static_cast<float>(exact));
+                const float v = b < n ? hi : tf32_round_host(static_cast<float>(exact - static_cast<double>(hi)));
+                f[(kk / 4) * lbo_floats + (b / 8) * 32 + (b % 8) * 4 + kk % 4] = v;
+            }
+        }
+    });
+}
+
 const float2* turn(long long total, int count)
 {
     return get(Key{2, total, count}, count, [&](std::vector<float2>& t) {

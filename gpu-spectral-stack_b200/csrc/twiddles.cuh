@@ -42,4 +42,11 @@ const float2* turn(long long total, int count);
 constexpr int kTf32DftOutputs = 16;
 const float2* tf32_dft_rows(int n, int m);
 
+// The row operand of the tensor-core pruned inverse (pruned_tc.cu): for output position j of an
+// n-point real row (n <= 256), 32 TF32 values cos(2 pi k j / n) (k = 0 .. 15), then
+// sin(2 pi k j / n) (k = 0 .. 15); rows 0 .. n-1 hold the hi parts, rows n .. 2n-1 the lo parts.
+// Canonical K-major layout without swizzle: value (row b, kk) at float
+// (kk / 4) (2n / 8) 32 + (b / 8) 32 + (b % 8) 4 + kk % 4. 64 n floats, returned as float2 storage.
+const float2* tf32_idft_rows(int n);
+
 }  // namespace spectral::twiddles

@@ -60,6 +60,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spectral_rfft2_modes": (_i, [_s, _p, _p, _i, _i, _i, _i, _ll, _p, _p]),
     "spectral_rfft2_modes_method": (_i, [_s, _p, _p, _i, _i, _i, _i, _ll, _i, _p, _p]),
     "spectral_irfft2_modes": (_i, [_s, _p, _p, _i, _i, _i, _i, _ll, _p, _p]),
+    "spectral_irfft2_modes_method": (_i, [_s, _p, _p, _i, _i, _i, _i, _ll, _i, _p, _p]),
     "spectral_slab_rows": (_i, [_p, _p, _i, _ll, _i, _i, _p]),
     "spectral_slab_columns": (_i, [_p, _p, _i, _i, _i, _p]),
     "spectral_slab_rows_peer": (_i, [_p, _p, ctypes.POINTER(_p), _i, _ll, _i, _i, _i, _p]),

@@ -181,6 +181,13 @@ SPECTRAL_API int spectral_rfft2_modes_method(const char* impl, const float* x, v
 /* The inverse: every other mode zero, then irfft2 (spectral.reference.irfft2_from_modes). */
 SPECTRAL_API int spectral_irfft2_modes(const char* impl, const void* modes, float* y, int n1, int n2, int m1,
                           int m2, long long batch, void* work, void* stream);
+/* spectral_irfft2_modes with the method chosen by the caller (no reference counterpart), as
+ * spectral_rfft2_modes_method: SPECTRAL_MODES_TENSOR runs the columns by the FFT engine and each
+ * real row as a GEMM with the kept columns' cosines and sines on the tcgen05 tensor cores (split
+ * TF32). Needs an engine implementation, n1 = n2 = 128, m2 <= 16 and a 16-byte aligned y. */
+SPECTRAL_API int spectral_irfft2_modes_method(const char* impl, const void* modes, float* y, int n1, int n2,
+                                              int m1, int m2, long long batch, int method, void* work,
+                                              void* stream);
 
 /* --- the large single-field 2D transform, slab-decomposed over ranks --------------------------- */
 /* An n x n complex field (n a power of two up to 16384) whose rows are split over `ranks` GPUs

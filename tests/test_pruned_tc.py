@@ -1,4 +1,4 @@
-"""The pruned 2D real forward by method: the FP32 engine (rows and columns by FFT passes) and the
+"""The pruned 2D real transforms by method: the FP32 engine (rows and columns by FFT passes) and the
 tensor-core method (the rows' kept DFT outputs as a split-TF32 GEMM on tcgen05, the columns by the
 engine), each against the float64 oracle (spectral.reference.rfft2_truncate) at the FFT
 tolerance, with the kept modes' own norm as the reference's tests/test_pruned.py normalises it,
@@ -11,7 +11,8 @@ import pytest
 import torch
 
 from oracle import reference as ref
-from oracle.policy import assert_truncated_close, fft_tolerance, random_real, relative_error
+from oracle.policy import (assert_transform_close, assert_truncated_close, fft_tolerance, random_complex, random_real,
+                           relative_error)
 from spectral import native
 
 AUTO, FP32, TENSOR = 0, 1, 2
@@ -96,3 +97,63 @@ def test_method_argument_checks():
                         None)
     with pytest.raises(ValueError, match="tensor-core method needs"):  # no fused kernel behind "naive"
         native.call("spectral_rfft2_modes_method", b"naive", 4096, 1 << 20, N, N, 16, 16, 4, TENSOR, 1 << 24, None)
+
+
+# --- the inverse ------------------------------------------------------------------------------------
+
+
+def inverse_by(modes: torch.Tensor, method: int, impl: bytes = b"stockham_r8") -> torch.Tensor:
+    fields, rows, m2 = modes.shape
+    y = torch.empty((fields, N, N), dtype=torch.float32, device=modes.device)
+    native.call("spectral_irfft2_modes_method", impl, modes.data_ptr(), y.data_ptr(), N, N, rows // 2, m2, fields,
+                method, None, torch.cuda.current_stream().cuda_stream)
+    return y
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(("fields", "m1", "m2"), CASES)
+@pytest.mark.parametrize("method", [FP32, TENSOR])
+def test_inverse_methods_match_the_oracle(rng, fields, m1, m2, method):
+    # Random modes, the DC column's imaginary parts included: the real inverse drops them, as
+    # numpy's irfft2 does.
+    modes = random_complex(rng, (fields, 2 * m1, m2))
+    y = inverse_by(torch.from_numpy(modes).cuda(), method).cpu().numpy()
+    assert_transform_close(y, ref.irfft2_from_modes(modes, (N, N)), N * N, axes=(-2, -1))
+    assert native.device_faults(clear=False) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("impl", [b"stockham_r2", b"stockham_r4", b"stockham_r8", b"stockham_r8_table"])
+def test_inverse_tensor_method_serves_every_engine_name(rng, impl):
+    modes = random_complex(rng, (33, 32, 16))
+    y = inverse_by(torch.from_numpy(modes).cuda(), TENSOR, impl).cpu().numpy()
+    assert_transform_close(y, ref.irfft2_from_modes(modes, (N, N)), N * N, axes=(-2, -1))
+
+
+@pytest.mark.gpu
+def test_inverse_methods_agree_the_tensor_method_repeats_and_round_trips(rng):
+    x = torch.from_numpy(random_real(rng, (512, N, N))).cuda()
+    modes = modes_by(x, 16, 16, TENSOR)
+    a = inverse_by(modes, TENSOR)
+    b = inverse_by(modes, TENSOR)
+    c = inverse_by(modes, FP32)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert_transform_close(a.cpu().numpy(), c.cpu().numpy().astype(np.float64), N * N, axes=(-2, -1),
+                           tol=2 * fft_tolerance(N * N))
+    # Forward of the inverse, against the oracle's: not the modes themselves, since a DC-column
+    # mode whose conjugate partner was not kept (kx = -m1) comes back halved by the real inverse.
+    again = modes_by(a, 16, 16, TENSOR).cpu().numpy()
+    expected = ref.rfft2_truncate(ref.irfft2_from_modes(modes.cpu().numpy(), (N, N)), 16, 16)
+    assert own_norm_error(again, expected) <= 2 * fft_tolerance(N * N)
+    assert native.device_faults(clear=False) == 0
+
+
+def test_inverse_method_argument_checks():
+    with pytest.raises(ValueError, match="method must be"):
+        native.call("spectral_irfft2_modes_method", b"stockham_r8", 4096, 8192, N, N, 16, 16, 4, 3, None, None)
+    for n1, n2, m1, m2, y in [(64, 128, 16, 16, 8192), (128, 256, 16, 16, 8192), (128, 128, 16, 17, 8192),
+                              (128, 128, 16, 16, 8200)]:
+        with pytest.raises(ValueError, match="tensor-core method needs"):
+            native.call("spectral_irfft2_modes_method", b"stockham_r8", 4096, y, n1, n2, m1, m2, 4, TENSOR, None,
+                        None)

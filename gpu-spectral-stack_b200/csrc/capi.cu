@@ -320,7 +320,7 @@ std::size_t c2c_pruned_work(const Impl& impl, int n, int, long long batch)
 // Whether spectral_rfft2_modes / spectral_irfft2_modes take the tensor-core kernels
 // (pruned_tc.cu) where they fit.
 constexpr bool kAutoTensorModes = true;
-constexpr bool kAutoTensorInverse = false;
+constexpr bool kAutoTensorInverse = true;
 
 bool fused_pruned(const Impl& impl, int n1, int n2, int m1, int m2)
 {

@@ -83,6 +83,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--sweep-out", default="", help="--sweep: CSV path (default: standard output)")
     p.add_argument("--sweep-ops", default="all", help="--sweep: comma-separated operations, or all")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--method", choices=["auto", "fp32", "tensor"], default="auto",
+                   help="pruned workload: the pruned transforms' row method (spectral_rfft2_modes_method); "
+                        "auto is what spectral_rfft2_modes uses")
     return p.parse_args()
 
 
@@ -287,8 +290,12 @@ class Pruned:
 
     name = "FNO layer: rfft2_truncated + mode_contract + irfft2_from_modes, 64x64x128x128 f32 (configs[3])"
 
-    def __init__(self, impl: str, samples: int = 64, channels: int = 64, n: int = 128, m: int = 16):
+    METHODS = {"auto": 0, "fp32": 1, "tensor": 2}  # SPECTRAL_MODES_*
+
+    def __init__(self, impl: str, samples: int = 64, channels: int = 64, n: int = 128, m: int = 16,
+                 method: str = "auto"):
         self.impl, self.samples, self.channels, self.n, self.m = impl, samples, channels, n, m
+        self.method = method
         self.fields = samples * channels
         self.bytes_per_call = self.fields * (4 * n * n + 16 * m * m)
         modes = 2 * m * m
@@ -322,21 +329,22 @@ class Pruned:
                 ("irfft2_modes", self.bytes_per_call)]
 
     def launches_per_step(self) -> int:
-        return 5  # pruned rows + pruned columns, the contraction, pruned columns + pruned rows
+        return 3  # the pruned forward, the contraction, the pruned inverse: one kernel each
 
     def launch(self, native, sets, k, stream, which):
         x, modes, mixed, _ = sets[k % SETS]
         _, _, mixed_old, y = sets[(k + 2) % SETS]
         imp = self.impl.encode()
+        method = self.METHODS[self.method]
         if which == 0:
-            native.call("spectral_rfft2_modes", imp, x.data_ptr(), modes.data_ptr(), self.n, self.n,
-                        self.m, self.m, self.fields, self.work.data_ptr(), stream)
+            native.call("spectral_rfft2_modes_method", imp, x.data_ptr(), modes.data_ptr(), self.n, self.n,
+                        self.m, self.m, self.fields, method, self.work.data_ptr(), stream)
         elif which == 1:
             native.call("spectral_mode_contract", modes.data_ptr(), self.weights.data_ptr(),
                         mixed.data_ptr(), self.samples, self.channels, self.channels, 2 * self.m * self.m, stream)
         else:
-            native.call("spectral_irfft2_modes", imp, mixed_old.data_ptr(), y.data_ptr(), self.n, self.n,
-                        self.m, self.m, self.fields, self.work.data_ptr(), stream)
+            native.call("spectral_irfft2_modes_method", imp, mixed_old.data_ptr(), y.data_ptr(), self.n, self.n,
+                        self.m, self.m, self.fields, method, self.work.data_ptr(), stream)
 
     def api_step(self, spectral, x_dev):
         modes = spectral.rfft2_truncated(x_dev, self.m, self.m, impl=self.impl)
@@ -895,7 +903,7 @@ def make_workload(args):
         wl = C2c(args.fft_impl, batch=1, n=1 << 24)
         wl.name = "fft_c2c fwd+inv of one 2^24-point c64 signal"
         return wl
-    return Pruned(args.fft_impl)
+    return Pruned(args.fft_impl, method=args.method)
 
 
 # --- parity of the timed outputs ------------------------------------------------------------------
@@ -1358,7 +1366,8 @@ def run_ours(args) -> None:
         "config": {"workload": wl.name, "fft_impl": args.fft_impl, "points_per_gpu": 1 << 24,
                    "parallelism": f"batch-sharded x{world}, no communication",
                    "l2": "4 rotating buffer sets (6x L2); inverse reads a spectrum written 2 steps earlier",
-                   "pct_hbm_peak": round(100 * value / world / peak, 2)},
+                   "pct_hbm_peak": round(100 * value / world / peak, 2),
+                   **({"pruned_method": args.method} if args.workload == "pruned" else {})},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": rounds * args.steps * wl.launches_per_step(),
         "clocks": clocks.summary(), "timing": timing, "parity": parity, "device_faults": faults,

@@ -186,7 +186,19 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32])
         : "r"(taddr));
 }
 
-__device__ __forceinline__ void tmem_wait_load() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Waits for this thread's tensor-memory loads. The registers a load wrote are in-out operands of
+// the wait, so the compiler places every use of them after it.
+__device__ __forceinline__ void tmem_wait_load(uint32_t (&r)[32])
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
 
 // Stores 32 consecutive 32-bit columns of this warp's 32 TMEM lanes, one lane per thread.
 __device__ __forceinline__ void tmem_store32(uint32_t taddr, const uint32_t (&r)[32])
@@ -243,13 +255,14 @@ __device__ __forceinline__ bool column_group(uint64_t* dfull, uint64_t* dempty, 
         const uint32_t acc = tmem + lane_base + static_cast<uint32_t>(G) * kDCols;
         tmem_load32(acc + 32, a);    // x_hi cos_lo (0-15), x_hi (-sin)_lo (16-31)
         tmem_load32(acc + 64, b);    // x_lo cos_hi, x_lo (-sin)_hi
-        tmem_wait_load();
+        tmem_wait_load(a);
+        tmem_wait_load(b);
 #pragma unroll
         for (int k = 0; k < 32; ++k) {
             a[k] = __float_as_uint(__uint_as_float(a[k]) + __uint_as_float(b[k]));
         }
         tmem_load32(acc, b);         // x_hi cos_hi, x_hi (-sin)_hi
-        tmem_wait_load();
+        tmem_wait_load(b);
         fence_before_sync();
         __syncwarp();
         if (lane == 0) {
@@ -737,7 +750,7 @@ __global__ void __launch_bounds__(kIThreads, 1)
                 engine::exchange_sync<1, kIEpiSync>();
                 uint32_t v[32];
                 tmem_load32(tmem + lane_base + static_cast<uint32_t>(d) * kIDCols + 32 * c, v);
-                tmem_wait_load();
+                tmem_wait_load(v);
                 if (c == kIOutBufs - 1) {
                     fence_before_sync();
                     __syncwarp();

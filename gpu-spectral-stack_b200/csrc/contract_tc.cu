@@ -238,7 +238,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     contract_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                        float2* __restrict__ out, int cin, int cout, long long modes, unsigned* fault)
 {
-    wait_for_previous_grid();
     allow_next_grid();
     extern __shared__ unsigned char smem_base[];
     // 1 KiB alignment for the operand planes (the descriptors need 16 bytes; TMA 128).
@@ -280,6 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
+    // The set-up above reads only host-built tables and this CTA's own resources, so it overlaps
+    // the previous kernel's tail; from here on global data another kernel may write is touched.
+    wait_for_previous_grid();
 
     bool failed = false;
     int loaded = 0;  // chunks whose TMA loads warp 0 has issued

@@ -305,7 +305,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                              long long fields, int m1, int m2, const float2* __restrict__ f_rows,
                              const float2* __restrict__ twc_g, unsigned* fault)
 {
-    wait_for_previous_grid();
     allow_next_grid();
     extern __shared__ unsigned char smem_base[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -359,6 +358,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
+    // The set-up above reads only host-built tables and this CTA's own resources, so it overlaps
+    // the previous kernel's tail; from here on global data another kernel may write is touched.
+    wait_for_previous_grid();
 
     const long long bx = blockIdx.x;
     const long long nf = fields > bx ? (fields - 1 - bx) / gridDim.x + 1 : 0;  // this CTA's fields
@@ -646,7 +648,6 @@ __global__ void __launch_bounds__(kIThreads, 1)
                              long long fields, int m1, int m2, const float2* __restrict__ f_rows,
                              const float2* __restrict__ twc_g, unsigned* fault)
 {
-    wait_for_previous_grid();
     allow_next_grid();
     extern __shared__ unsigned char smem_base[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -692,6 +693,9 @@ __global__ void __launch_bounds__(kIThreads, 1)
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
+    // The set-up above reads only host-built tables and this CTA's own resources, so it overlaps
+    // the previous kernel's tail; from here on global data another kernel may write is touched.
+    wait_for_previous_grid();
 
     const long long bx = blockIdx.x;
     const long long nf = fields > bx ? (fields - 1 - bx) / gridDim.x + 1 : 0;

@@ -18,6 +18,11 @@
  * Workspaces: the 2D, pruned and (for "naive") real entry points take a caller-allocated `work`
  * buffer whose size in complex values the matching *_workspace function reports (0 means NULL
  * is accepted), as the reference's fft2d.hpp:27-36 and pruned.hpp:26-36 do.
+ *
+ * Tables: the first call on a device that needs a given twiddle table (or, for the tensor-core
+ * pruned transforms, a DFT operand table) builds it in the library's static device pool with a
+ * synchronous copy, as the reference's twiddle_table() does (csrc/fft/twiddles.cu:17-46); make
+ * that first call before any CUDA graph capture on the device.
  */
 #ifndef SPECTRAL_B200_H
 #define SPECTRAL_B200_H

@@ -611,6 +611,10 @@ int spectral_rfft2_modes_method(const char* impl, const float* x, void* modes, i
         need_aligned(modes, "rfft2_modes");
         check_pruned_2d(i, n1, n2, m1, m2, batch);
         need_work(work, rfft2_modes_work(i, n1, n2, m1, m2, batch), "rfft2_modes");
+        // The kernels read x through the read-only path (or TMA) while modes are written.
+        need(!overlap(x, count3(batch, n1, n2) * sizeof(float), modes,
+                      count3(batch, 2 * m1, m2) * sizeof(float2)),
+             "rfft2_modes: x and modes must not overlap");
         auto* ms = static_cast<float2*>(modes);
         auto* ws = static_cast<float2*>(work);
         const cudaStream_t s = as_stream(stream);
@@ -656,6 +660,9 @@ int spectral_irfft2_modes_method(const char* impl, const void* modes, float* y, 
         need_aligned(y, "irfft2_modes");
         check_pruned_2d(i, n1, n2, m1, m2, batch);
         need_work(work, irfft2_modes_work(i, n1, n2, m1, m2, batch), "irfft2_modes");
+        need(!overlap(modes, count3(batch, 2 * m1, m2) * sizeof(float2), y,
+                      count3(batch, n1, n2) * sizeof(float)),
+             "irfft2_modes: modes and y must not overlap");
         const auto* ms = static_cast<const float2*>(modes);
         auto* ws = static_cast<float2*>(work);
         const cudaStream_t s = as_stream(stream);

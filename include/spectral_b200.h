@@ -165,7 +165,8 @@ SPECTRAL_API int spectral_rfft2_modes_workspace(const char* impl, int n1, int n2
 SPECTRAL_API int spectral_irfft2_modes_workspace(const char* impl, int n1, int n2, int m1, int m2,
                                     long long batch, size_t* count);
 /* The (2 m1) x m2 low-frequency modes of each rfft2 of n1 x n2 real values: rows 0 .. m1-1, then
- * n1-m1 .. n1-1; columns 0 .. m2-1 (spectral.reference.rfft2_truncate). */
+ * n1-m1 .. n1-1; columns 0 .. m2-1 (spectral.reference.rfft2_truncate). Out of place: x and
+ * modes (and, for the inverse below, modes and y) must not overlap. */
 SPECTRAL_API int spectral_rfft2_modes(const char* impl, const float* x, void* modes, int n1, int n2, int m1,
                          int m2, long long batch, void* work, void* stream);
 /* spectral_rfft2_modes with the row stage's method chosen by the caller (no reference

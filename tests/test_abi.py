@@ -162,6 +162,10 @@ def test_slab_relayout_argument_checks():
         ("spectral_slab_rows", (4096, 4096, 8, 8, 1, 1, None)),
         ("spectral_slab_columns", (4096, 4104, 8, 8, 0, None)),
         ("spectral_slab_columns", (4096 + 8 * 63, 4096, 8, 8, 1, None)),
+        # Pruned 2D transforms of 2 fields of 16 x 16, 4 x 4 modes: x is 2048 bytes, modes 512.
+        ("spectral_rfft2_modes", (b"stockham_r8", 4096, 4096 + 2040, 16, 16, 2, 4, 2, None, None)),
+        ("spectral_irfft2_modes", (b"stockham_r8", 4096 + 2040, 4096, 16, 16, 2, 4, 2, None, None)),
+        ("spectral_rfft2_modes_method", (b"stockham_r8", 4096, 4096, 16, 16, 2, 4, 2, 1, None, None)),
     ],
 )
 def test_overlapping_input_and_output_ranges_are_refused(fn, args):

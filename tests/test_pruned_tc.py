@@ -151,9 +151,9 @@ def test_inverse_methods_agree_the_tensor_method_repeats_and_round_trips(rng):
 
 def test_inverse_method_argument_checks():
     with pytest.raises(ValueError, match="method must be"):
-        native.call("spectral_irfft2_modes_method", b"stockham_r8", 4096, 8192, N, N, 16, 16, 4, 3, None, None)
-    for n1, n2, m1, m2, y in [(64, 128, 16, 16, 8192), (128, 256, 16, 16, 8192), (128, 128, 16, 17, 8192),
-                              (128, 128, 16, 16, 8200)]:
+        native.call("spectral_irfft2_modes_method", b"stockham_r8", 4096, 1 << 20, N, N, 16, 16, 4, 3, None, None)
+    for n1, n2, m1, m2, y in [(64, 128, 16, 16, 1 << 20), (128, 256, 16, 16, 1 << 20), (128, 128, 16, 17, 1 << 20),
+                              (128, 128, 16, 16, (1 << 20) + 8)]:
         with pytest.raises(ValueError, match="tensor-core method needs"):
             native.call("spectral_irfft2_modes_method", b"stockham_r8", 4096, y, n1, n2, m1, m2, 4, TENSOR, None,
                         None)
